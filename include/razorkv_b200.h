@@ -1,0 +1,203 @@
+/*
+ * razorkv_b200 -- C ABI of the B200 (sm_100a) RazorKV decode path.
+ *
+ * Every entry point takes plain device pointers, element strides and sizes, enqueues its
+ * work on the given CUDA stream (passed as void*, a cudaStream_t; NULL = legacy default
+ * stream) and returns an rkv_status.  Nothing here allocates, frees or synchronises: the
+ * caller owns every buffer, including the workspaces whose sizes the *_workspace_size
+ * queries report, and all sizes needed for a launch are host-known.  Calls are
+ * stream-ordered; the library keeps no per-call state, so calls from several host threads
+ * on different streams are independent.
+ *
+ * Reference interfaces replaced (paths inside the reference project):
+ *   rkv_decode_attention      razorkv/kernels/triton_paged_sparse.py:105-174
+ *                             (triton_paged_sparse_attention) and, with page_table == NULL,
+ *                             razorkv/kernels/torch_sparse.py:15-61 (compacted_paged_sdpa)
+ *   rkv_page_salience_pool    razorkv/kernels/torch_sparse.py:64-93 (compute_page_salience_pool)
+ *   rkv_append                razorkv/cache.py:239-247 (_init_salience) and :369-390
+ *                             (the append half of RazorKVCache.update)
+ *   rkv_score                 razorkv/cache.py:249-287 (update_salience_with_query)
+ *   rkv_decode_fused          razorkv/cache.py:392-393 followed by the attention call of a
+ *                             non-compacting decode step (score and attend in one K pass)
+ *   rkv_page_scores           razorkv/cache.py:322-331 (haystack page max-pool)
+ *   rkv_select_pages          razorkv/cache.py:333-341 (batch mean, top-k, ascending sort)
+ *   rkv_compact_pages         razorkv/cache.py:343-359 when the sink is page aligned
+ *                             (page-table rewrite + free-list push, no data movement)
+ *   rkv_compact_tokens        razorkv/cache.py:310-320 and :343-359 in general (token copy)
+ *   rkv_release_pages         the storage release implied by razorkv/cache.py:356-358
+ *   rkv_gather_tokens         materialises the contiguous key_cache/value_cache tensors of
+ *                             razorkv/cache.py:89-91 from the paged layout
+ */
+#ifndef RAZORKV_B200_H
+#define RAZORKV_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum rkv_status {
+    RKV_OK = 0,
+    RKV_ERR_INVALID_ARGUMENT = 1,   /* null pointer, negative or inconsistent size */
+    RKV_ERR_UNSUPPORTED = 2,        /* shape / dtype combination not implemented */
+    RKV_ERR_WORKSPACE_TOO_SMALL = 3,
+    RKV_ERR_FREE_LIST_EXHAUSTED = 4,
+    RKV_ERR_ALIGNMENT = 5,          /* pointer or stride misaligned for the vector path */
+    RKV_ERR_CUDA = 6,               /* launch or runtime error */
+    RKV_ERR_PAGE_OUT_OF_RANGE = 7   /* host-visible page index outside the pool */
+} rkv_status;
+
+typedef enum rkv_dtype { RKV_F32 = 0, RKV_F16 = 1, RKV_BF16 = 2 } rkv_dtype;
+
+typedef enum rkv_pool { RKV_POOL_MAX = 0, RKV_POOL_MEAN = 1 } rkv_pool;
+
+typedef enum rkv_salience_init { RKV_SAL_NORM = 0, RKV_SAL_UNIFORM = 1 } rkv_salience_init;
+
+/* Key/value storage of one layer.  Row (b, h, t) -- D contiguous elements -- starts at
+ *   base + b*stride_b + h*stride_h + page_table[b*pt_stride_b + t/page_size]*stride_p
+ *        + (t % page_size)*stride_t
+ * or, with page_table == NULL, at base + b*stride_b + h*stride_h + t*stride_t.
+ * Strides are in elements.  For the reference's paged operator the storage is
+ * [B, Hkv, MAXP, P, D]; for the cache pool it is [slots, B, Hkv, P, D] with one page table
+ * shared by all sequences (pt_stride_b = 0). */
+typedef struct rkv_kv_layout {
+    const void* k;
+    const void* v;               /* may be NULL for score-only calls */
+    int32_t dtype;               /* rkv_dtype of k and v */
+    int32_t head_dim;            /* D */
+    int64_t batch;               /* B */
+    int64_t num_kv_heads;        /* Hkv */
+    int64_t stride_b, stride_h, stride_p, stride_t;
+    int64_t page_size;           /* tokens per physical page */
+    int64_t num_slots;           /* physical pages in the storage */
+    const int64_t* page_table;   /* NULL = contiguous tokens */
+    int64_t pt_stride_b;         /* 0 = table shared by every sequence */
+    int64_t num_tokens;          /* valid tokens per sequence */
+} rkv_kv_layout;
+
+/* Query rows [B, Hq, QL, D]: element (b, h, t, d) at q + b*stride_b + h*stride_h + t*stride_t + d. */
+typedef struct rkv_query {
+    const void* q;
+    int32_t dtype;
+    int32_t num_heads;           /* Hq, a multiple of Hkv */
+    int64_t q_len;               /* QL */
+    int64_t stride_b, stride_h, stride_t;
+} rkv_query;
+
+/* Attention output [B, Hq, QL, D], same addressing as rkv_query. */
+typedef struct rkv_output {
+    void* out;
+    int32_t dtype;
+    int32_t reserved;
+    int64_t stride_b, stride_h, stride_t;
+} rkv_output;
+
+/* fp32 token salience.  Score of (b, t) at
+ *   s + page_table[t/page_size]*stride_p + b*stride_b + t % page_size      (paged), or
+ *   s + b*stride_b + t                                                   (page_table NULL),
+ * using the page table and page size of the rkv_kv_layout it is passed with. */
+typedef struct rkv_salience {
+    float* s;
+    int64_t stride_b;
+    int64_t stride_p;
+} rkv_salience;
+
+const char* rkv_status_string(int status);
+int rkv_abi_version(void);
+
+/* ---- attention --------------------------------------------------------------------------
+ * out = softmax(q.k * scale) . v over the num_tokens tokens of each (b, kv-head), GQA head
+ * h reading kv head h / (Hq/Hkv).  causal != 0 masks key t > query row (upper-left aligned).
+ * scale <= 0 selects 1/sqrt(D).  fp32 accumulation; the output is rounded to out->dtype. */
+size_t rkv_decode_attention_workspace_size(const rkv_query* q, const rkv_kv_layout* kv);
+int rkv_decode_attention(const rkv_query* q, const rkv_kv_layout* kv, float scale, int causal,
+                         const rkv_output* out, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
+/* ---- page pooling -----------------------------------------------------------------------
+ * out[b, p] = max (or mean) of sal[b*stride_b + p*page_size + i], i < page_size, for
+ * p < S / page_size (when S < page_size: out[b, 0] = max over the row). */
+int rkv_page_salience_pool(const float* sal, int64_t batch, int64_t seq_len, int64_t stride_b,
+                           int64_t page_size, int pool_type, float* out, void* stream);
+
+/* ---- cache: append ------------------------------------------------------------------------
+ * Writes n_new tokens (rows k_new/v_new [B, Hkv, n_new, D] with the given element strides)
+ * at logical positions [pos, pos + n_new) of the layer described by kv (k and v are written),
+ * and their initial salience (||k||_2 averaged over kv heads, or 1.0).  Every logical page
+ * that starts inside the range takes the physical page free_stack[free_top - 1 - i] (i-th
+ * new page) and records it in page_table (writable, shared by all sequences); the caller
+ * then lowers its free-stack top by the number of new pages. */
+int rkv_append(const rkv_kv_layout* kv, const rkv_salience* sal, const void* k_new,
+               const void* v_new, int64_t new_stride_b, int64_t new_stride_h,
+               int64_t new_stride_t, int64_t n_new, int64_t pos, int64_t* page_table,
+               const int64_t* free_stack, int64_t free_top, int salience_init, void* stream);
+
+/* ---- cache: salience --------------------------------------------------------------------
+ * R[b, t] = max over query rows (h, r) of the canonical fp32 dot fl(q*scale_r) . k[b, h/G, t];
+ * then S = fl(fl(decay*S) + fl(one_minus_decay*R)) when ewma != 0, else S = R.
+ * scale_r = 1/sqrt(D) rounded to fp32 (the reference's fixed resonance scale). */
+int rkv_score(const rkv_query* q, const rkv_kv_layout* kv, const rkv_salience* sal,
+              float decay, float one_minus_decay, int ewma, void* stream);
+
+/* Score (as rkv_score with ewma = 1, q_len = 1) and attention (as rkv_decode_attention,
+ * causal = 0) from one pass over K. */
+size_t rkv_decode_fused_workspace_size(const rkv_query* q, const rkv_kv_layout* kv);
+int rkv_decode_fused(const rkv_query* q, const rkv_kv_layout* kv, const rkv_salience* sal,
+                     float decay, float one_minus_decay, float scale, const rkv_output* out,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- cache: selection --------------------------------------------------------------------
+ * scores[b, p] = max over i < sel_page_size of S(b, first_token + p*sel_page_size + i),
+ * p < num_pages, written with row stride num_pages. */
+int rkv_page_scores(const rkv_kv_layout* kv, const rkv_salience* sal, int64_t first_token,
+                    int64_t num_pages, int64_t sel_page_size, float* scores, void* stream);
+
+/* kept[0..k) = the k pages with the largest batch mean of scores[b, p] (sequential fp32
+ * sum over b = 0..batch-1, then one division; batch == 1 uses the row itself), exact ties to
+ * the lower page index, in ascending page order.  margin (optional, one float) receives
+ * mean[k-th] - mean[(k+1)-th] in selection order (+inf when k == num_pages). */
+size_t rkv_select_pages_workspace_size(int64_t num_pages);
+int rkv_select_pages(const float* scores, int64_t batch, int64_t num_pages, int64_t k,
+                     int64_t* kept, float* margin, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/* ---- cache: compaction -------------------------------------------------------------------
+ * Pointer-only compaction of a shared page table whose haystack pages are
+ * [sink_pages, sink_pages + num_pages): the table becomes
+ *   table[0:sink_pages] ++ table[sink_pages + kept[i]] ++ table[tail_first_page:n_pages_total]
+ * and the dropped haystack pages are pushed, in ascending logical order, at
+ * free_stack[free_top ...]; the caller raises its free-stack top by num_pages - k. */
+int rkv_compact_pages(int64_t* page_table, int64_t sink_pages, int64_t num_pages,
+                      const int64_t* kept, int64_t k, int64_t tail_first_page,
+                      int64_t n_pages_total, int64_t* free_stack, int64_t free_top,
+                      void* stream);
+
+/* Copying compaction.  New logical token i < new_len takes old token
+ *   i                                          for i < sink,
+ *   hay_start + kept[j / P]*P + j % P          for j = i - sink < k*P  (P = sel_page_size),
+ *   tail_src_start + (i - sink - k*P)          otherwise,
+ * of the layer kv (old table), written through new_page_table whose pages are popped as
+ * new_page_table[i] = free_stack[free_top - 1 - i].  K, V and salience move together. */
+int rkv_compact_tokens(const rkv_kv_layout* kv, const rkv_salience* sal,
+                       int64_t* new_page_table, const int64_t* free_stack, int64_t free_top,
+                       int64_t new_len, int64_t sink, const int64_t* kept, int64_t k,
+                       int64_t sel_page_size, int64_t hay_start, int64_t tail_src_start,
+                       void* stream);
+
+/* free_stack[free_top + i] = pages[i], i < n. */
+int rkv_release_pages(const int64_t* pages, int64_t n, int64_t* free_stack, int64_t free_top,
+                      void* stream);
+
+/* dst[b, h, t, :] = row (b, h, t) of kv (K when which == 0, V when 1), t < num_tokens;
+ * dst is contiguous [B, Hkv, num_tokens, D] of kv->dtype.  sal_dst (optional, [B, num_tokens])
+ * receives the salience. */
+int rkv_gather_tokens(const rkv_kv_layout* kv, int which, void* dst, const rkv_salience* sal,
+                      float* sal_dst, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RAZORKV_B200_H */

@@ -1,0 +1,321 @@
+// C-ABI entry points of librazorkv_b200.so: argument validation, path choice, launch.
+// Every function returns an rkv_status and never allocates, frees or synchronises.
+#include <math.h>
+
+#include "../../include/razorkv_b200.h"
+#include "rkv_common.cuh"
+#include "rkv_kernels.h"
+
+using namespace rkv;
+
+namespace {
+
+inline cudaStream_t S(void* s) { return static_cast<cudaStream_t>(s); }
+
+inline int status_of(cudaError_t e) {
+    if (e == cudaSuccess) return RKV_OK;
+    if (e == cudaErrorNotSupported) return RKV_ERR_UNSUPPORTED;
+    return RKV_ERR_CUDA;
+}
+
+inline bool dtype_ok(int d) { return d == RKV_F32 || d == RKV_F16 || d == RKV_BF16; }
+
+int check_kv(const rkv_kv_layout* kv, bool need_v) {
+    if (!kv || !kv->k || (need_v && !kv->v)) return RKV_ERR_INVALID_ARGUMENT;
+    if (!dtype_ok(kv->dtype)) return RKV_ERR_UNSUPPORTED;
+    if (kv->head_dim < 1 || kv->head_dim > kMaxHeadDim) return RKV_ERR_UNSUPPORTED;
+    if (kv->batch < 0 || kv->num_kv_heads < 1 || kv->num_tokens < 0) return RKV_ERR_INVALID_ARGUMENT;
+    if (kv->page_table && kv->page_size < 1) return RKV_ERR_INVALID_ARGUMENT;
+    return RKV_OK;
+}
+
+int check_q(const rkv_query* q, const rkv_kv_layout* kv) {
+    if (!q || !q->q) return RKV_ERR_INVALID_ARGUMENT;
+    if (!dtype_ok(q->dtype)) return RKV_ERR_UNSUPPORTED;
+    if (q->num_heads < 1 || q->num_heads % kv->num_kv_heads != 0) return RKV_ERR_INVALID_ARGUMENT;
+    if (q->q_len < 1) return RKV_ERR_INVALID_ARGUMENT;
+    return RKV_OK;
+}
+
+float resonance_scale(int D) { return (float)(1.0 / sqrt((double)D)); }
+
+AttnParams attn_params(const rkv_query* q, const rkv_kv_layout* kv, float scale, int causal,
+                       const rkv_output* out) {
+    AttnParams p{};
+    p.q = q->q; p.q_dtype = q->dtype;
+    p.q_stride_b = q->stride_b; p.q_stride_h = q->stride_h; p.q_stride_t = q->stride_t;
+    p.Hq = q->num_heads; p.QL = (int)q->q_len;
+    p.k = kv->k; p.v = kv->v; p.kv_dtype = kv->dtype; p.D = kv->head_dim;
+    p.Hkv = (int)kv->num_kv_heads; p.B = kv->batch; p.N = kv->num_tokens;
+    p.stride_b = kv->stride_b; p.stride_h = kv->stride_h; p.stride_p = kv->stride_p;
+    p.stride_t = kv->stride_t; p.page_size = kv->page_size;
+    p.page_table = kv->page_table; p.pt_stride_b = kv->pt_stride_b;
+    p.scale = scale > 0.0f ? scale : (float)(1.0 / sqrt((double)kv->head_dim));
+    p.causal = causal;
+    p.out = out->out; p.out_dtype = out->dtype;
+    p.o_stride_b = out->stride_b; p.o_stride_h = out->stride_h; p.o_stride_t = out->stride_t;
+    return p;
+}
+
+bool fast_ok(const rkv_query* q, const rkv_kv_layout* kv, bool need_v) {
+    if (q->q_len != 1) return false;
+    if (!kv->page_table) return false;
+    return fused_supported(kv->dtype, kv->head_dim, (int)kv->num_kv_heads, q->num_heads,
+                           kv->page_size, kv->stride_t, kv->stride_h, kv->stride_b,
+                           kv->stride_p, kv->k, need_v ? kv->v : kv->k) &&
+           q->dtype == kv->dtype;
+}
+
+FusedParams fused_params(const rkv_query* q, const rkv_kv_layout* kv, const rkv_salience* sal,
+                         float decay, float omd, float scale, const rkv_output* out) {
+    FusedParams p{};
+    p.q = q->q; p.q_stride_b = q->stride_b; p.q_stride_h = q->stride_h;
+    p.Hq = q->num_heads; p.Hkv = (int)kv->num_kv_heads; p.D = kv->head_dim;
+    p.B = kv->batch; p.N = kv->num_tokens;
+    p.k = kv->k; p.v = kv->v;
+    p.stride_b = kv->stride_b; p.stride_h = kv->stride_h; p.stride_p = kv->stride_p;
+    p.stride_t = kv->stride_t; p.num_slots = kv->num_slots;
+    p.page_table = kv->page_table; p.pt_stride_b = kv->pt_stride_b;
+    p.sal = sal ? sal->s : nullptr;
+    p.sal_stride_b = sal ? sal->stride_b : 0; p.sal_stride_p = sal ? sal->stride_p : 0;
+    p.scale_r = resonance_scale(kv->head_dim);
+    const float sc = scale > 0.0f ? scale : p.scale_r;
+    p.logit_mul = sc / p.scale_r;
+    p.decay = decay; p.one_minus_decay = omd;
+    p.attend = out ? 1 : 0;
+    if (out) { p.out = out->out; p.o_stride_b = out->stride_b; p.o_stride_h = out->stride_h; }
+    return p;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* rkv_status_string(int s) {
+    switch (s) {
+        case RKV_OK: return "ok";
+        case RKV_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case RKV_ERR_UNSUPPORTED: return "unsupported shape or dtype";
+        case RKV_ERR_WORKSPACE_TOO_SMALL: return "workspace too small";
+        case RKV_ERR_FREE_LIST_EXHAUSTED: return "free page list exhausted";
+        case RKV_ERR_ALIGNMENT: return "misaligned pointer or stride";
+        case RKV_ERR_CUDA: return "CUDA launch or runtime error";
+        case RKV_ERR_PAGE_OUT_OF_RANGE: return "page index out of range";
+        default: return "unknown status";
+    }
+}
+
+int rkv_abi_version(void) { return 1; }
+
+size_t rkv_decode_attention_workspace_size(const rkv_query* q, const rkv_kv_layout* kv) {
+    if (!q || !kv) return 0;
+    const int64_t G = q->num_heads / (kv->num_kv_heads > 0 ? kv->num_kv_heads : 1);
+    int splits = attn_num_splits(kv->num_tokens, kv->batch, kv->num_kv_heads, G * q->q_len);
+    size_t generic = attn_workspace_floats(kv->batch, q->num_heads, q->q_len, kv->head_dim, splits) *
+                     sizeof(float);
+    size_t fast = fused_workspace_bytes(kv->batch, q->num_heads, kv->head_dim);
+    return generic > fast ? generic : fast;
+}
+
+int rkv_decode_attention(const rkv_query* q, const rkv_kv_layout* kv, float scale, int causal,
+                         const rkv_output* out, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+    int st = check_kv(kv, true);
+    if (st) return st;
+    if ((st = check_q(q, kv))) return st;
+    if (!out || !out->out || !dtype_ok(out->dtype)) return RKV_ERR_INVALID_ARGUMENT;
+    if (kv->batch == 0) return RKV_OK;
+    if (workspace_bytes < rkv_decode_attention_workspace_size(q, kv) || !workspace)
+        return RKV_ERR_WORKSPACE_TOO_SMALL;
+    if (!causal && kv->num_tokens > 0 && fast_ok(q, kv, true)) {
+        FusedParams p = fused_params(q, kv, nullptr, 0.f, 0.f, scale, out);
+        p.partials = static_cast<float*>(workspace);
+        return status_of(launch_fused(p, S(stream)));
+    }
+    AttnParams p = attn_params(q, kv, scale, causal, out);
+    const int64_t G = q->num_heads / kv->num_kv_heads;
+    p.num_splits = attn_num_splits(kv->num_tokens, kv->batch, kv->num_kv_heads, G * q->q_len);
+    p.workspace = static_cast<float*>(workspace);
+    return status_of(launch_attention(p, S(stream)));
+}
+
+int rkv_page_salience_pool(const float* sal, int64_t batch, int64_t seq_len, int64_t stride_b,
+                           int64_t page_size, int pool_type, float* out, void* stream) {
+    if (!sal || !out || batch < 0 || seq_len < 1 || page_size < 1) return RKV_ERR_INVALID_ARGUMENT;
+    if (pool_type != RKV_POOL_MAX && pool_type != RKV_POOL_MEAN) return RKV_ERR_INVALID_ARGUMENT;
+    if (seq_len < page_size) pool_type = RKV_POOL_MAX;   // the reference returns the row max
+    return status_of(launch_pool(sal, batch, seq_len, stride_b, page_size,
+                                 pool_type == RKV_POOL_MEAN, out, S(stream)));
+}
+
+int rkv_append(const rkv_kv_layout* kv, const rkv_salience* sal, const void* k_new,
+               const void* v_new, int64_t new_stride_b, int64_t new_stride_h,
+               int64_t new_stride_t, int64_t n_new, int64_t pos, int64_t* page_table,
+               const int64_t* free_stack, int64_t free_top, int salience_init, void* stream) {
+    int st = check_kv(kv, true);
+    if (st) return st;
+    if (!sal || !sal->s || !k_new || !v_new || !page_table || !free_stack) return RKV_ERR_INVALID_ARGUMENT;
+    if (n_new < 0 || pos < 0 || free_top < 0) return RKV_ERR_INVALID_ARGUMENT;
+    const int64_t P = kv->page_size;
+    const int64_t first_new = (pos + P - 1) / P;
+    const int64_t last_page = (pos + n_new + P - 1) / P;   // exclusive
+    const int64_t need = last_page > first_new ? last_page - first_new : 0;
+    if (need > free_top) return RKV_ERR_FREE_LIST_EXHAUSTED;
+    AppendParams p{};
+    p.k = const_cast<void*>(kv->k); p.v = const_cast<void*>(kv->v); p.dtype = kv->dtype;
+    p.D = kv->head_dim; p.Hkv = (int)kv->num_kv_heads; p.B = kv->batch;
+    p.stride_b = kv->stride_b; p.stride_h = kv->stride_h; p.stride_p = kv->stride_p;
+    p.stride_t = kv->stride_t; p.page_size = P;
+    p.sal = sal->s; p.sal_stride_b = sal->stride_b; p.sal_stride_p = sal->stride_p;
+    p.k_new = k_new; p.v_new = v_new;
+    p.new_stride_b = new_stride_b; p.new_stride_h = new_stride_h; p.new_stride_t = new_stride_t;
+    p.n_new = n_new; p.pos = pos;
+    p.page_table = page_table; p.free_stack = free_stack; p.free_top = free_top;
+    p.salience_init = salience_init;
+    return status_of(launch_append(p, S(stream)));
+}
+
+int rkv_score(const rkv_query* q, const rkv_kv_layout* kv, const rkv_salience* sal,
+              float decay, float one_minus_decay, int ewma, void* stream) {
+    int st = check_kv(kv, false);
+    if (st) return st;
+    if ((st = check_q(q, kv))) return st;
+    if (!sal || !sal->s) return RKV_ERR_INVALID_ARGUMENT;
+    if (kv->batch == 0 || kv->num_tokens == 0) return RKV_OK;
+    if (ewma && fast_ok(q, kv, false)) {
+        FusedParams p = fused_params(q, kv, sal, decay, one_minus_decay, 0.f, nullptr);
+        return status_of(launch_fused(p, S(stream)));
+    }
+    ScoreParams p{};
+    p.q = q->q; p.q_dtype = q->dtype;
+    p.q_stride_b = q->stride_b; p.q_stride_h = q->stride_h; p.q_stride_t = q->stride_t;
+    p.Hq = q->num_heads; p.QL = (int)q->q_len;
+    p.k = kv->k; p.kv_dtype = kv->dtype; p.D = kv->head_dim; p.Hkv = (int)kv->num_kv_heads;
+    p.B = kv->batch; p.N = kv->num_tokens;
+    p.stride_b = kv->stride_b; p.stride_h = kv->stride_h; p.stride_p = kv->stride_p;
+    p.stride_t = kv->stride_t; p.page_size = kv->page_size;
+    p.page_table = kv->page_table; p.pt_stride_b = kv->pt_stride_b;
+    p.sal = sal->s; p.sal_stride_b = sal->stride_b; p.sal_stride_p = sal->stride_p;
+    p.scale_r = resonance_scale(kv->head_dim);
+    p.decay = decay; p.one_minus_decay = one_minus_decay; p.ewma = ewma;
+    return status_of(launch_score(p, S(stream)));
+}
+
+size_t rkv_decode_fused_workspace_size(const rkv_query* q, const rkv_kv_layout* kv) {
+    return rkv_decode_attention_workspace_size(q, kv);
+}
+
+int rkv_decode_fused(const rkv_query* q, const rkv_kv_layout* kv, const rkv_salience* sal,
+                     float decay, float one_minus_decay, float scale, const rkv_output* out,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+    int st = check_kv(kv, true);
+    if (st) return st;
+    if ((st = check_q(q, kv))) return st;
+    if (!sal || !sal->s || !out || !out->out) return RKV_ERR_INVALID_ARGUMENT;
+    if (q->q_len != 1) return RKV_ERR_UNSUPPORTED;
+    if (kv->batch == 0) return RKV_OK;
+    if (workspace_bytes < rkv_decode_fused_workspace_size(q, kv) || !workspace)
+        return RKV_ERR_WORKSPACE_TOO_SMALL;
+    if (kv->num_tokens > 0 && fast_ok(q, kv, true)) {
+        FusedParams p = fused_params(q, kv, sal, decay, one_minus_decay, scale, out);
+        p.partials = static_cast<float*>(workspace);
+        return status_of(launch_fused(p, S(stream)));
+    }
+    // shapes outside the fused kernel: the two shape-general kernels back to back
+    if ((st = rkv_score(q, kv, sal, decay, one_minus_decay, 1, stream))) return st;
+    return rkv_decode_attention(q, kv, scale, 0, out, workspace, workspace_bytes, stream);
+}
+
+int rkv_page_scores(const rkv_kv_layout* kv, const rkv_salience* sal, int64_t first_token,
+                    int64_t num_pages, int64_t sel_page_size, float* scores, void* stream) {
+    if (!kv || !sal || !sal->s || !scores) return RKV_ERR_INVALID_ARGUMENT;
+    if (first_token < 0 || num_pages < 0 || sel_page_size < 1) return RKV_ERR_INVALID_ARGUMENT;
+    if (first_token + num_pages * sel_page_size > kv->num_tokens) return RKV_ERR_INVALID_ARGUMENT;
+    PageScoreParams p{};
+    p.sal = sal->s; p.sal_stride_b = sal->stride_b; p.sal_stride_p = sal->stride_p;
+    p.page_table = kv->page_table; p.page_size = kv->page_size;
+    p.B = kv->batch; p.first_token = first_token; p.num_pages = num_pages;
+    p.sel_page_size = sel_page_size; p.scores = scores;
+    return status_of(launch_page_scores(p, S(stream)));
+}
+
+size_t rkv_select_pages_workspace_size(int64_t num_pages) {
+    return (size_t)(num_pages > 0 ? num_pages : 1) * sizeof(uint32_t);
+}
+
+int rkv_select_pages(const float* scores, int64_t batch, int64_t num_pages, int64_t k,
+                     int64_t* kept, float* margin, void* workspace, size_t workspace_bytes,
+                     void* stream) {
+    if (!scores || !kept || batch < 1 || num_pages < 1 || k < 1 || k > num_pages)
+        return RKV_ERR_INVALID_ARGUMENT;
+    if (!workspace || workspace_bytes < rkv_select_pages_workspace_size(num_pages))
+        return RKV_ERR_WORKSPACE_TOO_SMALL;
+    return status_of(launch_select(scores, batch, num_pages, k, kept, margin,
+                                   static_cast<uint32_t*>(workspace), S(stream)));
+}
+
+int rkv_compact_pages(int64_t* page_table, int64_t sink_pages, int64_t num_pages,
+                      const int64_t* kept, int64_t k, int64_t tail_first_page,
+                      int64_t n_pages_total, int64_t* free_stack, int64_t free_top,
+                      void* stream) {
+    if (!page_table || !kept || !free_stack) return RKV_ERR_INVALID_ARGUMENT;
+    if (sink_pages < 0 || num_pages < 1 || k < 1 || k > num_pages || free_top < 0)
+        return RKV_ERR_INVALID_ARGUMENT;
+    if (tail_first_page != sink_pages + num_pages || n_pages_total < tail_first_page)
+        return RKV_ERR_INVALID_ARGUMENT;
+    return status_of(launch_compact_pages(page_table, sink_pages, num_pages, kept, k,
+                                          tail_first_page, n_pages_total, free_stack, free_top,
+                                          S(stream)));
+}
+
+int rkv_compact_tokens(const rkv_kv_layout* kv, const rkv_salience* sal,
+                       int64_t* new_page_table, const int64_t* free_stack, int64_t free_top,
+                       int64_t new_len, int64_t sink, const int64_t* kept, int64_t k,
+                       int64_t sel_page_size, int64_t hay_start, int64_t tail_src_start,
+                       void* stream) {
+    int st = check_kv(kv, true);
+    if (st) return st;
+    if (!kv->page_table || !sal || !sal->s || !new_page_table || !free_stack)
+        return RKV_ERR_INVALID_ARGUMENT;
+    if (k > 0 && !kept) return RKV_ERR_INVALID_ARGUMENT;
+    if (new_len < 0 || sink < 0 || k < 0 || sel_page_size < 1) return RKV_ERR_INVALID_ARGUMENT;
+    if (sink + k * sel_page_size > new_len) return RKV_ERR_INVALID_ARGUMENT;
+    if (tail_src_start + (new_len - sink - k * sel_page_size) > kv->num_tokens)
+        return RKV_ERR_INVALID_ARGUMENT;
+    const int64_t pages = (new_len + kv->page_size - 1) / kv->page_size;
+    if (pages > free_top) return RKV_ERR_FREE_LIST_EXHAUSTED;
+    CompactTokensParams p{};
+    p.k = const_cast<void*>(kv->k); p.v = const_cast<void*>(kv->v); p.dtype = kv->dtype;
+    p.D = kv->head_dim; p.Hkv = kv->num_kv_heads; p.B = kv->batch;
+    p.stride_b = kv->stride_b; p.stride_h = kv->stride_h; p.stride_p = kv->stride_p;
+    p.stride_t = kv->stride_t; p.page_size = kv->page_size;
+    p.sal = sal->s; p.sal_stride_b = sal->stride_b; p.sal_stride_p = sal->stride_p;
+    p.old_pt = kv->page_table; p.new_pt = new_page_table; p.free_stack = free_stack;
+    p.free_top = free_top; p.new_len = new_len; p.sink = sink; p.n_kept = k; p.kept = kept;
+    p.sel_page_size = sel_page_size; p.hay_start = hay_start; p.tail_src_start = tail_src_start;
+    return status_of(launch_compact_tokens(p, S(stream)));
+}
+
+int rkv_release_pages(const int64_t* pages, int64_t n, int64_t* free_stack, int64_t free_top,
+                      void* stream) {
+    if ((n > 0 && !pages) || !free_stack || n < 0 || free_top < 0) return RKV_ERR_INVALID_ARGUMENT;
+    return status_of(launch_release(pages, n, free_stack, free_top, S(stream)));
+}
+
+int rkv_gather_tokens(const rkv_kv_layout* kv, int which, void* dst, const rkv_salience* sal,
+                      float* sal_dst, void* stream) {
+    int st = check_kv(kv, which == 1);
+    if (st) return st;
+    if (!dst || (sal_dst && (!sal || !sal->s))) return RKV_ERR_INVALID_ARGUMENT;
+    GatherParams p{};
+    p.src = which == 1 ? kv->v : kv->k; p.dst = dst; p.dtype = kv->dtype;
+    p.B = kv->batch; p.Hkv = kv->num_kv_heads; p.N = kv->num_tokens; p.D = kv->head_dim;
+    p.stride_b = kv->stride_b; p.stride_h = kv->stride_h; p.stride_p = kv->stride_p;
+    p.stride_t = kv->stride_t; p.page_size = kv->page_size;
+    p.page_table = kv->page_table; p.pt_stride_b = kv->pt_stride_b;
+    p.sal = sal ? sal->s : nullptr; p.sal_stride_b = sal ? sal->stride_b : 0;
+    p.sal_stride_p = sal ? sal->stride_p : 0; p.sal_dst = sal_dst;
+    return status_of(launch_gather(p, S(stream)));
+}
+
+}  // extern "C"

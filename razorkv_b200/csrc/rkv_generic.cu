@@ -1,0 +1,607 @@
+// Shape-general kernels of the RazorKV decode path: any head_dim <= 256, any page size,
+// fp32 / fp16 / bf16, any query length.  They define the semantics the specialised sm_100a
+// decode kernel (rkv_decode_sm100.cu) must reproduce, and serve every shape it does not
+// cover.  All of them are HBM- or latency-bound scans; none is GEMM-shaped.
+#include <math.h>
+
+#include "rkv_common.cuh"
+#include "rkv_kernels.h"
+
+namespace rkv {
+
+// ------------------------------------------------------------------------------------------
+// Salience score (razorkv/cache.py:249-287)
+// ------------------------------------------------------------------------------------------
+// CTA = (token block of kScoreTokens tokens, sequence b).  256 threads = 32 groups of 8
+// lanes; group g handles tokens t0 + g + 32*i.  The query rows of one kv head are staged in
+// shared memory as fl(q * scale) (fp32); every group walks its tokens, loads the K row once
+// per kv head (lane j keeps the elements of chunks j, j+8, ...) and takes the canonical dot
+// with every query row of that head.
+constexpr int kScoreThreads = 256;
+constexpr int kScoreTokens = 128;   // 4 tokens per group
+constexpr int kScoreTPG = kScoreTokens / 32;
+constexpr int kLaneElts = 32;       // max elements one lane owns (D <= 256)
+
+__device__ __forceinline__ int lane_elements(int D, int ch, int j, int* idx) {
+    int n = 0;
+    for (int c = j; c * ch < D; c += 8)
+        for (int e = c * ch; e < min(D, c * ch + ch); ++e) idx[n++] = e;
+    return n;
+}
+
+__global__ void __launch_bounds__(kScoreThreads)
+score_kernel(ScoreParams p) {
+    extern __shared__ float qs[];   // [rows_per_chunk][D]
+    const int b = blockIdx.y;
+    const int lane = threadIdx.x & 31;
+    const int group = threadIdx.x >> 3;   // 0..31
+    const int j = lane & 7;
+    const int D = p.D;
+    const int ch = 16 / elt_bytes(p.kv_dtype);
+    const int G = p.Hq / p.Hkv;
+    const int64_t t0 = (int64_t)blockIdx.x * kScoreTokens;
+
+    int idx[kLaneElts];
+    const int ne = lane_elements(D, ch, j, idx);
+
+    uint32_t best[kScoreTPG];
+#pragma unroll
+    for (int i = 0; i < kScoreTPG; ++i) best[i] = 0u;   // below every ordered key
+
+    const int rows_per_head = G * p.QL;
+    const int chunk_rows = p.rows_per_chunk;
+    const float scale = p.scale_r;
+    TokenMap tm{p.page_table ? p.page_table + (int64_t)b * p.pt_stride_b : nullptr,
+                p.page_size, p.stride_p, p.stride_t};
+
+    for (int h = 0; h < p.Hkv; ++h) {
+        for (int r0 = 0; r0 < rows_per_head; r0 += chunk_rows) {
+            const int nr = min(chunk_rows, rows_per_head - r0);
+            __syncthreads();
+            for (int i = threadIdx.x; i < nr * D; i += blockDim.x) {
+                int r = r0 + i / D, d = i % D;
+                int hq = h * G + r / p.QL, tq = r % p.QL;
+                float qv = load_elt(p.q, (int64_t)b * p.q_stride_b + (int64_t)hq * p.q_stride_h +
+                                             (int64_t)tq * p.q_stride_t + d, p.q_dtype);
+                qs[i] = __fmul_rn(qv, scale);
+            }
+            __syncthreads();
+            // every lane runs the same number of group8_sum shuffles; tokens past N are
+            // computed on zeros and discarded
+            for (int it = 0; it < kScoreTPG; ++it) {
+                const int64_t t = t0 + group + 32 * it;
+                const bool valid = t < p.N;
+                float kr[kLaneElts];
+                if (valid) {
+                    const int64_t row = (int64_t)b * p.stride_b + (int64_t)h * p.stride_h + tm.offset(t);
+                    for (int e = 0; e < ne; ++e) kr[e] = load_elt(p.k, row + idx[e], p.kv_dtype);
+                } else {
+                    for (int e = 0; e < ne; ++e) kr[e] = 0.0f;
+                }
+                for (int r = 0; r < nr; ++r) {
+                    float acc = 0.0f;
+                    const float* qr = qs + r * D;
+                    for (int e = 0; e < ne; ++e) acc = __fmaf_rn(qr[idx[e]], kr[e], acc);
+                    const float s = group8_sum(acc);
+                    if (valid) best[it] = max(best[it], ordered_key(s));
+                }
+            }
+        }
+    }
+    if (j == 0) {
+        for (int it = 0; it < kScoreTPG; ++it) {
+            int64_t t = t0 + group + 32 * it;
+            if (t >= p.N) break;
+            float R = key_to_float(best[it]);
+            float* sp = p.sal + (p.page_table ? tm.page_table[t / p.page_size] * p.sal_stride_p +
+                                                    (int64_t)b * p.sal_stride_b + t % p.page_size
+                                              : (int64_t)b * p.sal_stride_b + t);
+            *sp = p.ewma ? __fadd_rn(__fmul_rn(p.decay, *sp), __fmul_rn(p.one_minus_decay, R)) : R;
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// Attention, split over tokens (razorkv/kernels/triton_paged_sparse.py:23-102 semantics:
+// online softmax over the pages of the table; razorkv/kernels/torch_sparse.py:15-61 for the
+// contiguous case).  CTA = (split, b*Hkv + kvh, block of 4 query rows); one warp per query
+// row; lanes split D (element e = lane + 32*i).  Partials (m, l, acc[D]) go to the workspace
+// and merge_kernel combines them.
+// ------------------------------------------------------------------------------------------
+constexpr int kAttnWarps = 4;
+
+__global__ void __launch_bounds__(kAttnWarps * 32)
+attn_split_kernel(AttnParams p) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int bh = blockIdx.y;
+    const int b = bh / p.Hkv, kvh = bh % p.Hkv;
+    const int G = p.Hq / p.Hkv;
+    const int row = blockIdx.z * kAttnWarps + warp;      // 0 .. G*QL-1
+    if (row >= G * p.QL) return;
+    const int hq = kvh * G + row / p.QL, tq = row % p.QL;
+    const int D = p.D;
+    const int split = blockIdx.x;
+    const int64_t per = (p.N + p.num_splits - 1) / p.num_splits;
+    const int64_t s0 = split * per;
+    int64_t s1 = (p.N < s0 + per ? p.N : s0 + per);
+    if (p.causal) { const int64_t lim = (int64_t)tq + 1; s1 = s1 < lim ? s1 : lim; };
+
+    float q[8], acc[8];
+    const int ne = (D + 31) / 32;
+    for (int i = 0; i < 8; ++i) {
+        int e = lane + 32 * i;
+        q[i] = (i < ne && e < D)
+                   ? load_elt(p.q, (int64_t)b * p.q_stride_b + (int64_t)hq * p.q_stride_h +
+                                       (int64_t)tq * p.q_stride_t + e, p.q_dtype)
+                   : 0.0f;
+        acc[i] = 0.0f;
+    }
+    float m = -INFINITY, l = 0.0f;
+    TokenMap tm{p.page_table ? p.page_table + (int64_t)b * p.pt_stride_b : nullptr,
+                p.page_size, p.stride_p, p.stride_t};
+    const int64_t base = (int64_t)b * p.stride_b + (int64_t)kvh * p.stride_h;
+    for (int64_t t = s0; t < s1; ++t) {
+        const int64_t off = base + tm.offset(t);
+        float part = 0.0f;
+        for (int i = 0; i < ne; ++i) {
+            int e = lane + 32 * i;
+            if (e < D) part = fmaf(q[i], load_elt(p.k, off + e, p.kv_dtype), part);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+        const float s = part * p.scale;
+        const float mn = fmaxf(m, s);
+        const float alpha = __expf(m - mn);
+        const float pw = __expf(s - mn);
+        l = l * alpha + pw;
+        for (int i = 0; i < ne; ++i) {
+            int e = lane + 32 * i;
+            float v = e < D ? load_elt(p.v, off + e, p.kv_dtype) : 0.0f;
+            acc[i] = acc[i] * alpha + pw * v;
+        }
+        m = mn;
+    }
+    // workspace layout: [split][b][hq][tq] -> {m, l, acc[D]}
+    const int64_t slot = (((int64_t)split * p.B + b) * p.Hq + hq) * p.QL + tq;
+    float* w = p.workspace + slot * (D + 2);
+    if (lane == 0) { w[0] = m; w[1] = l; }
+    for (int i = 0; i < ne; ++i) {
+        int e = lane + 32 * i;
+        if (e < D) w[2 + e] = acc[i];
+    }
+}
+
+__global__ void merge_kernel(AttnParams p) {
+    // one CTA per (b, hq, tq); threads over D
+    const int64_t r = blockIdx.x;
+    const int tq = r % p.QL;
+    const int hq = (r / p.QL) % p.Hq;
+    const int b = r / ((int64_t)p.QL * p.Hq);
+    const int D = p.D;
+    float M = -INFINITY;
+    for (int s = 0; s < p.num_splits; ++s) {
+        const float* w = p.workspace + ((((int64_t)s * p.B + b) * p.Hq + hq) * p.QL + tq) * (D + 2);
+        M = fmaxf(M, w[0]);
+    }
+    float L = 0.0f;
+    for (int s = 0; s < p.num_splits; ++s) {
+        const float* w = p.workspace + ((((int64_t)s * p.B + b) * p.Hq + hq) * p.QL + tq) * (D + 2);
+        if (w[0] != -INFINITY) L += w[1] * __expf(w[0] - M);
+    }
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        float o = 0.0f;
+        for (int s = 0; s < p.num_splits; ++s) {
+            const float* w =
+                p.workspace + ((((int64_t)s * p.B + b) * p.Hq + hq) * p.QL + tq) * (D + 2);
+            if (w[0] != -INFINITY) o += w[2 + d] * __expf(w[0] - M);
+        }
+        store_elt(p.out, (int64_t)b * p.o_stride_b + (int64_t)hq * p.o_stride_h +
+                             (int64_t)tq * p.o_stride_t + d, p.out_dtype, L > 0.0f ? o / L : 0.0f);
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// Page pooling (razorkv/kernels/torch_sparse.py:64-93) and haystack page scores
+// (razorkv/cache.py:322-331).  NaN propagates like torch.amax.
+// ------------------------------------------------------------------------------------------
+__global__ void pool_kernel(const float* sal, int64_t B, int64_t S, int64_t stride_b, int64_t P,
+                            int64_t n_pages, int mean, float* out) {
+    int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= B * n_pages) return;
+    int64_t b = i / n_pages, pg = i % n_pages;
+    const float* row = sal + b * stride_b;
+    if (S < P) {   // fewer tokens than one page: the reference returns the row max
+        uint32_t best = 0u;
+        for (int64_t t = 0; t < S; ++t) best = max(best, ordered_key(row[t]));
+        out[i] = key_to_float(best);
+        return;
+    }
+    if (mean) {
+        float acc = 0.0f;
+        for (int64_t t = 0; t < P; ++t) acc = __fadd_rn(acc, row[pg * P + t]);
+        out[i] = __fdiv_rn(acc, (float)P);
+    } else {
+        uint32_t best = 0u;
+        for (int64_t t = 0; t < P; ++t) best = max(best, ordered_key(row[pg * P + t]));
+        out[i] = key_to_float(best);
+    }
+}
+
+__global__ void page_scores_kernel(PageScoreParams p) {
+    int64_t pg = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    int b = blockIdx.y;
+    if (pg >= p.num_pages) return;
+    uint32_t best = 0u;
+    for (int64_t i = 0; i < p.sel_page_size; ++i) {
+        int64_t t = p.first_token + pg * p.sel_page_size + i;
+        const float* sp = p.sal + (p.page_table ? p.page_table[t / p.page_size] * p.sal_stride_p +
+                                                     (int64_t)b * p.sal_stride_b + t % p.page_size
+                                               : (int64_t)b * p.sal_stride_b + t);
+        best = max(best, ordered_key(*sp));
+    }
+    p.scores[(int64_t)b * p.num_pages + pg] = key_to_float(best);
+}
+
+// ------------------------------------------------------------------------------------------
+// Top-k page selection (razorkv/cache.py:333-341) -- one CTA.
+// mean[p] = (sum_b scores[b, p] in ascending b) / B; radix select of the k-th largest
+// ordered key over four 8-bit digits; keys equal to the threshold are taken lowest index
+// first; kept pages are emitted in ascending order by a block scan.
+// ------------------------------------------------------------------------------------------
+constexpr int kSelThreads = 1024;
+
+__device__ __forceinline__ int block_exclusive_scan(int v, int* warp_sums, int* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_sums[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int w = lane < (blockDim.x >> 5) ? warp_sums[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            int y = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += y;
+        }
+        warp_sums[lane] = w;   // inclusive
+    }
+    __syncthreads();
+    int res = x - v + (warp > 0 ? warp_sums[warp - 1] : 0);
+    if (total) *total = warp_sums[(blockDim.x >> 5) - 1];
+    __syncthreads();
+    return res;
+}
+
+__global__ void __launch_bounds__(kSelThreads)
+select_kernel(const float* scores, int64_t B, int64_t n, int64_t k, int64_t* kept, float* margin,
+              uint32_t* keys) {
+    __shared__ int hist[256];
+    __shared__ int warp_sums[32];
+    __shared__ uint32_t s_prefix;
+    __shared__ int s_remaining;
+    __shared__ uint32_t s_best_out;
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+        float acc = scores[i];
+        if (B > 1) {
+            for (int64_t b = 1; b < B; ++b) acc = __fadd_rn(acc, scores[b * n + i]);
+            acc = __fdiv_rn(acc, (float)B);
+        }
+        keys[i] = ordered_key(acc);
+    }
+    if (threadIdx.x == 0) { s_prefix = 0u; s_remaining = (int)k; s_best_out = 0u; }
+    __syncthreads();
+    uint32_t mask = 0u;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+        __syncthreads();
+        const uint32_t prefix = s_prefix;
+        for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+            uint32_t key = keys[i];
+            if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            int cum = 0, rem = s_remaining;
+            for (int d = 255; d >= 0; --d) {
+                if (cum + hist[d] >= rem) {
+                    s_prefix = prefix | ((uint32_t)d << shift);
+                    s_remaining = rem - cum;
+                    break;
+                }
+                cum += hist[d];
+            }
+        }
+        mask |= 255u << shift;
+        __syncthreads();
+    }
+    const uint32_t thr = s_prefix;
+    const int need_eq = s_remaining;   // how many keys equal to thr are kept (lowest index first)
+    int eq_base = 0, out_base = 0;
+    for (int64_t c = 0; c < n; c += blockDim.x) {
+        int64_t i = c + threadIdx.x;
+        uint32_t key = i < n ? keys[i] : 0u;
+        int is_eq = (i < n && key == thr) ? 1 : 0;
+        int eq_total;
+        int eq_rank = eq_base + block_exclusive_scan(is_eq, warp_sums, &eq_total);
+        int take = (i < n) && (key > thr || (is_eq && eq_rank < need_eq)) ? 1 : 0;
+        if (i < n && !take) atomicMax(&s_best_out, key);
+        int out_total;
+        int pos = out_base + block_exclusive_scan(take, warp_sums, &out_total);
+        if (take && pos < k) kept[pos] = i;
+        eq_base += eq_total;
+        out_base += out_total;
+    }
+    __syncthreads();
+    if (margin && threadIdx.x == 0) {
+        *margin = (k >= n) ? INFINITY : __fsub_rn(key_to_float(thr), key_to_float(s_best_out));
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// Pointer-only compaction (razorkv/cache.py:343-359 for a page-aligned sink).  One CTA.
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ int64_t lower_bound(const int64_t* a, int64_t n, int64_t x) {
+    int64_t lo = 0, hi = n;
+    while (lo < hi) {
+        int64_t mid = (lo + hi) >> 1;
+        if (a[mid] < x) lo = mid + 1; else hi = mid;
+    }
+    return lo;
+}
+
+__global__ void __launch_bounds__(1024)
+compact_pages_kernel(int64_t* pt, int64_t sink_pages, int64_t num_pages, const int64_t* kept,
+                     int64_t k, int64_t tail_first, int64_t n_total, int64_t* free_stack,
+                     int64_t free_top) {
+    // 1. push dropped haystack pages in ascending logical order
+    for (int64_t j = threadIdx.x; j < num_pages; j += blockDim.x) {
+        int64_t lb = lower_bound(kept, k, j);
+        bool is_kept = lb < k && kept[lb] == j;
+        if (!is_kept) free_stack[free_top + (j - lb)] = pt[sink_pages + j];
+    }
+    __syncthreads();
+    // 2. rewrite in place; destination index <= source index, chunk by chunk
+    const int64_t n_tail = n_total - tail_first;
+    const int64_t n_out = k + n_tail;
+    for (int64_t c = 0; c < n_out; c += blockDim.x) {
+        int64_t i = c + threadIdx.x;
+        int64_t v = 0;
+        if (i < n_out) v = i < k ? pt[sink_pages + kept[i]] : pt[tail_first + (i - k)];
+        __syncthreads();
+        if (i < n_out) pt[sink_pages + i] = v;
+        __syncthreads();
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// Append (razorkv/cache.py:239-247, 369-390): write rows, initial salience, new page ids.
+// One 8-lane group per (b, token); the group copies the K and V rows of every kv head and
+// reduces sum_h sqrt(canonical k.k) in ascending h.
+// ------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+append_kernel(AppendParams p) {
+    const int lane = threadIdx.x & 31, j = lane & 7;
+    const int64_t gidx = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 3;
+    const bool active = gidx < p.n_new * p.B;
+    const int64_t b = active ? gidx / p.n_new : 0;
+    const int64_t i = active ? gidx % p.n_new : 0;
+    const int64_t t = p.pos + i;
+    const int64_t P = p.page_size;
+    const int64_t first_new_page = (p.pos + P - 1) / P;
+    const int64_t lp = t / P;
+    int64_t phys = 0;
+    if (active) {
+        phys = lp < first_new_page ? p.page_table[lp]
+                                   : p.free_stack[p.free_top - 1 - (lp - first_new_page)];
+        if (b == 0 && j == 0 && lp >= first_new_page && t % P == 0) p.page_table[lp] = phys;
+    }
+    const int ch = 16 / elt_bytes(p.dtype);
+    int idx[kLaneElts];
+    const int ne = lane_elements(p.D, ch, j, idx);
+    float norm_sum = 0.0f;
+    for (int h = 0; h < p.Hkv; ++h) {
+        float part = 0.0f;
+        if (active) {
+            const int64_t src = b * p.new_stride_b + (int64_t)h * p.new_stride_h + i * p.new_stride_t;
+            const int64_t dst = b * p.stride_b + (int64_t)h * p.stride_h + phys * p.stride_p +
+                                (t % P) * p.stride_t;
+            for (int e = 0; e < ne; ++e) {
+                float kv = load_elt(p.k_new, src + idx[e], p.dtype);
+                store_elt(p.k, dst + idx[e], p.dtype, kv);
+                store_elt(p.v, dst + idx[e], p.dtype, load_elt(p.v_new, src + idx[e], p.dtype));
+                part = __fmaf_rn(kv, kv, part);
+            }
+        }
+        float ss = group8_sum(part);
+        norm_sum = __fadd_rn(norm_sum, __fsqrt_rn(ss));
+    }
+    if (active && j == 0) {
+        float s0 = p.salience_init == RKV_SAL_NORM ? __fdiv_rn(norm_sum, (float)p.Hkv) : 1.0f;
+        p.sal[phys * p.sal_stride_p + b * p.sal_stride_b + t % P] = s0;
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// Copying compaction (razorkv/cache.py:310-320, 343-359 in general).
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ int64_t compact_source(const CompactTokensParams& p, int64_t i) {
+    if (i < p.sink) return i;
+    int64_t j = i - p.sink;
+    int64_t P = p.sel_page_size;
+    if (j < p.n_kept * P) return p.hay_start + p.kept[j / P] * P + j % P;
+    return p.tail_src_start + (j - p.n_kept * P);
+}
+
+__global__ void compact_tokens_kernel(CompactTokensParams p) {
+    // one thread per (b, h, new token, element-chunk of 4)
+    const int64_t D = p.D;
+    const int64_t nd = (D + 3) / 4;
+    int64_t gid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int64_t total = p.new_len * p.B * p.Hkv * nd;
+    if (gid >= total) return;
+    const int64_t dq = gid % nd;
+    int64_t r = gid / nd;
+    const int64_t i = r % p.new_len; r /= p.new_len;
+    const int64_t h = r % p.Hkv;
+    const int64_t b = r / p.Hkv;
+    const int64_t P = p.page_size;
+    const int64_t src_t = compact_source(p, i);
+    const int64_t src_pg = p.old_pt[src_t / P];
+    const int64_t dst_pg = p.free_stack[p.free_top - 1 - i / P];
+    if (b == 0 && h == 0 && dq == 0 && i % P == 0) p.new_pt[i / P] = dst_pg;
+    const int64_t so = b * p.stride_b + h * p.stride_h + src_pg * p.stride_p + (src_t % P) * p.stride_t;
+    const int64_t dof = b * p.stride_b + h * p.stride_h + dst_pg * p.stride_p + (i % P) * p.stride_t;
+    const int eb = elt_bytes(p.dtype);
+    for (int64_t e = dq * 4; e < min(D, dq * 4 + 4); ++e) {
+        if (eb == 4) {
+            static_cast<float*>(p.k)[dof + e] = static_cast<const float*>(p.k)[so + e];
+            static_cast<float*>(p.v)[dof + e] = static_cast<const float*>(p.v)[so + e];
+        } else {
+            static_cast<uint16_t*>(p.k)[dof + e] = static_cast<const uint16_t*>(p.k)[so + e];
+            static_cast<uint16_t*>(p.v)[dof + e] = static_cast<const uint16_t*>(p.v)[so + e];
+        }
+    }
+    if (h == 0 && dq == 0) {
+        p.sal[dst_pg * p.sal_stride_p + b * p.sal_stride_b + i % P] =
+            p.sal[src_pg * p.sal_stride_p + b * p.sal_stride_b + src_t % P];
+    }
+}
+
+__global__ void release_kernel(const int64_t* pages, int64_t n, int64_t* free_stack, int64_t top) {
+    int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i < n) free_stack[top + i] = pages[i];
+}
+
+// ------------------------------------------------------------------------------------------
+// Materialise contiguous [B, Hkv, N, D] rows (and [B, N] salience) from the paged layout.
+// ------------------------------------------------------------------------------------------
+__global__ void gather_kernel(GatherParams p) {
+    int64_t gid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int64_t total = p.B * p.Hkv * p.N * p.D;
+    if (gid >= total) return;
+    const int64_t d = gid % p.D;
+    int64_t r = gid / p.D;
+    const int64_t t = r % p.N; r /= p.N;
+    const int64_t h = r % p.Hkv;
+    const int64_t b = r / p.Hkv;
+    TokenMap tm{p.page_table ? p.page_table + b * p.pt_stride_b : nullptr, p.page_size,
+                p.stride_p, p.stride_t};
+    const int64_t off = b * p.stride_b + h * p.stride_h + tm.offset(t) + d;
+    if (elt_bytes(p.dtype) == 4)
+        static_cast<float*>(p.dst)[gid] = static_cast<const float*>(p.src)[off];
+    else
+        static_cast<uint16_t*>(p.dst)[gid] = static_cast<const uint16_t*>(p.src)[off];
+    if (p.sal_dst && h == 0 && d == 0) {
+        const float* sp = p.sal + (p.page_table ? tm.page_table[t / p.page_size] * p.sal_stride_p +
+                                                     b * p.sal_stride_b + t % p.page_size
+                                               : b * p.sal_stride_b + t);
+        p.sal_dst[b * p.N + t] = *sp;
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// launchers
+// ------------------------------------------------------------------------------------------
+cudaError_t launch_score(const ScoreParams& p, cudaStream_t st) {
+    ScoreParams q = p;
+    const int rows = (q.Hq / q.Hkv) * q.QL;
+    const int max_rows = (48 * 1024) / (q.D * 4);
+    q.rows_per_chunk = rows < max_rows ? rows : max_rows;
+    dim3 grid((unsigned)((q.N + kScoreTokens - 1) / kScoreTokens), (unsigned)q.B);
+    if (q.N == 0) return cudaSuccess;
+    score_kernel<<<grid, kScoreThreads, q.rows_per_chunk * q.D * sizeof(float), st>>>(q);
+    return cudaGetLastError();
+}
+
+int attn_num_splits(int64_t N, int64_t B, int64_t Hkv, int64_t rows) {
+    // aim for ~4 CTAs per SM over 148 SMs; at least 16 tokens per split
+    int64_t ctas = B * Hkv * ((rows + kAttnWarps - 1) / kAttnWarps);
+    int64_t want = (148 * 4 + ctas - 1) / ctas;
+    int64_t maxs = (N + 15) / 16;
+    if (want > maxs) want = maxs;
+    if (want < 1) want = 1;
+    if (want > 256) want = 256;
+    return (int)want;
+}
+
+size_t attn_workspace_floats(int64_t B, int64_t Hq, int64_t QL, int64_t D, int splits) {
+    return (size_t)splits * B * Hq * QL * (D + 2);
+}
+
+cudaError_t launch_attention(const AttnParams& p, cudaStream_t st) {
+    const int rows = (p.Hq / p.Hkv) * p.QL;
+    dim3 grid((unsigned)p.num_splits, (unsigned)(p.B * p.Hkv),
+              (unsigned)((rows + kAttnWarps - 1) / kAttnWarps));
+    attn_split_kernel<<<grid, kAttnWarps * 32, 0, st>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    merge_kernel<<<(unsigned)(p.B * p.Hq * p.QL), 128, 0, st>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_pool(const float* sal, int64_t B, int64_t S, int64_t stride_b, int64_t P,
+                        int mean, float* out, cudaStream_t st) {
+    int64_t n_pages = S / P;
+    if (n_pages == 0) n_pages = 1;
+    int64_t total = B * n_pages;
+    if (total == 0) return cudaSuccess;
+    pool_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(sal, B, S, stride_b, P, n_pages,
+                                                                 mean, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_page_scores(const PageScoreParams& p, cudaStream_t st) {
+    if (p.num_pages == 0 || p.B == 0) return cudaSuccess;
+    dim3 grid((unsigned)((p.num_pages + 255) / 256), (unsigned)p.B);
+    page_scores_kernel<<<grid, 256, 0, st>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_select(const float* scores, int64_t B, int64_t n, int64_t k, int64_t* kept,
+                          float* margin, uint32_t* keys, cudaStream_t st) {
+    select_kernel<<<1, kSelThreads, 0, st>>>(scores, B, n, k, kept, margin, keys);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_compact_pages(int64_t* pt, int64_t sink_pages, int64_t num_pages,
+                                 const int64_t* kept, int64_t k, int64_t tail_first,
+                                 int64_t n_total, int64_t* free_stack, int64_t free_top,
+                                 cudaStream_t st) {
+    compact_pages_kernel<<<1, 1024, 0, st>>>(pt, sink_pages, num_pages, kept, k, tail_first,
+                                             n_total, free_stack, free_top);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_append(const AppendParams& p, cudaStream_t st) {
+    int64_t groups = p.n_new * p.B;
+    if (groups == 0) return cudaSuccess;
+    append_kernel<<<(unsigned)((groups * 8 + 255) / 256), 256, 0, st>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_compact_tokens(const CompactTokensParams& p, cudaStream_t st) {
+    int64_t total = p.new_len * p.B * p.Hkv * ((p.D + 3) / 4);
+    if (total == 0) return cudaSuccess;
+    compact_tokens_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_release(const int64_t* pages, int64_t n, int64_t* free_stack, int64_t top,
+                           cudaStream_t st) {
+    if (n == 0) return cudaSuccess;
+    release_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(pages, n, free_stack, top);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gather(const GatherParams& p, cudaStream_t st) {
+    int64_t total = p.B * p.Hkv * p.N * p.D;
+    if (total == 0) return cudaSuccess;
+    gather_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace rkv

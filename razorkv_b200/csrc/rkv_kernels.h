@@ -1,0 +1,105 @@
+// Kernel parameter blocks and launchers shared by the C-ABI layer (rkv_capi.cu) and the
+// kernel translation units.  Internal to the library.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace rkv {
+
+struct ScoreParams {
+    const void* q; int q_dtype; int64_t q_stride_b, q_stride_h, q_stride_t;
+    int Hq, QL;
+    const void* k; int kv_dtype; int D; int Hkv; int64_t B, N;
+    int64_t stride_b, stride_h, stride_p, stride_t, page_size;
+    const int64_t* page_table; int64_t pt_stride_b;
+    float* sal; int64_t sal_stride_b, sal_stride_p;
+    float scale_r, decay, one_minus_decay; int ewma;
+    int rows_per_chunk;
+};
+
+struct AttnParams {
+    const void* q; int q_dtype; int64_t q_stride_b, q_stride_h, q_stride_t;
+    int Hq, QL;
+    const void* k; const void* v; int kv_dtype; int D; int Hkv; int64_t B, N;
+    int64_t stride_b, stride_h, stride_p, stride_t, page_size;
+    const int64_t* page_table; int64_t pt_stride_b;
+    float scale; int causal;
+    void* out; int out_dtype; int64_t o_stride_b, o_stride_h, o_stride_t;
+    float* workspace; int num_splits;
+};
+
+struct PageScoreParams {
+    const float* sal; int64_t sal_stride_b, sal_stride_p;
+    const int64_t* page_table; int64_t page_size;
+    int64_t B, first_token, num_pages, sel_page_size;
+    float* scores;
+};
+
+struct AppendParams {
+    void* k; void* v; int dtype; int D; int Hkv; int64_t B;
+    int64_t stride_b, stride_h, stride_p, stride_t, page_size;
+    float* sal; int64_t sal_stride_b, sal_stride_p;
+    const void* k_new; const void* v_new; int64_t new_stride_b, new_stride_h, new_stride_t;
+    int64_t n_new, pos;
+    int64_t* page_table; const int64_t* free_stack; int64_t free_top;
+    int salience_init;
+};
+
+struct CompactTokensParams {
+    void* k; void* v; int dtype; int64_t D, Hkv, B;
+    int64_t stride_b, stride_h, stride_p, stride_t, page_size;
+    float* sal; int64_t sal_stride_b, sal_stride_p;
+    const int64_t* old_pt; int64_t* new_pt; const int64_t* free_stack; int64_t free_top;
+    int64_t new_len, sink, n_kept, sel_page_size, hay_start, tail_src_start;
+    const int64_t* kept;
+};
+
+struct GatherParams {
+    const void* src; void* dst; int dtype; int64_t B, Hkv, N, D;
+    int64_t stride_b, stride_h, stride_p, stride_t, page_size;
+    const int64_t* page_table; int64_t pt_stride_b;
+    const float* sal; int64_t sal_stride_b, sal_stride_p; float* sal_dst;
+};
+
+// Fused score + attention for the sm_100a fast path (rkv_decode_sm100.cu).
+struct FusedParams {
+    const void* q; int64_t q_stride_b, q_stride_h;
+    int Hq, Hkv, D; int64_t B, N;
+    const void* k; const void* v;
+    int64_t stride_b, stride_h, stride_p, stride_t, num_slots;
+    const int64_t* page_table; int64_t pt_stride_b;
+    float* sal; int64_t sal_stride_b, sal_stride_p;   // nullptr: attention only
+    float scale_r, logit_mul, decay, one_minus_decay;
+    int attend;                                        // 0: score only (no V, no output)
+    void* out; int64_t o_stride_b, o_stride_h;
+    float* partials; int* counters; int grid;
+};
+
+cudaError_t launch_score(const ScoreParams& p, cudaStream_t st);
+int attn_num_splits(int64_t N, int64_t B, int64_t Hkv, int64_t rows);
+size_t attn_workspace_floats(int64_t B, int64_t Hq, int64_t QL, int64_t D, int splits);
+cudaError_t launch_attention(const AttnParams& p, cudaStream_t st);
+cudaError_t launch_pool(const float* sal, int64_t B, int64_t S, int64_t stride_b, int64_t P,
+                        int mean, float* out, cudaStream_t st);
+cudaError_t launch_page_scores(const PageScoreParams& p, cudaStream_t st);
+cudaError_t launch_select(const float* scores, int64_t B, int64_t n, int64_t k, int64_t* kept,
+                          float* margin, uint32_t* keys, cudaStream_t st);
+cudaError_t launch_compact_pages(int64_t* pt, int64_t sink_pages, int64_t num_pages,
+                                 const int64_t* kept, int64_t k, int64_t tail_first,
+                                 int64_t n_total, int64_t* free_stack, int64_t free_top,
+                                 cudaStream_t st);
+cudaError_t launch_append(const AppendParams& p, cudaStream_t st);
+cudaError_t launch_compact_tokens(const CompactTokensParams& p, cudaStream_t st);
+cudaError_t launch_release(const int64_t* pages, int64_t n, int64_t* free_stack, int64_t top,
+                           cudaStream_t st);
+cudaError_t launch_gather(const GatherParams& p, cudaStream_t st);
+
+// fast path: returns cudaErrorNotSupported when the shape is outside its coverage
+bool fused_supported(int dtype, int D, int Hkv, int Hq, int64_t page_size, int64_t stride_t,
+                     int64_t stride_h, int64_t stride_b, int64_t stride_p, const void* k,
+                     const void* v);
+size_t fused_workspace_bytes(int64_t B, int Hq, int D);
+cudaError_t launch_fused(const FusedParams& p, cudaStream_t st);
+
+}  // namespace rkv

@@ -1,0 +1,109 @@
+"""Regenerate the golden fixtures by running the REFERENCE implementation.
+
+Usage (in a checkout where the reference project is available):
+
+    python tests/golden/make_golden.py /path/to/razorkv-reference
+
+For every case below the script draws the seeded synthetic workload with
+``razorkv_b200.workload`` (CPU generators, deterministic for a given torch build), drives
+the reference's own ``RazorKVCache.update(..., {"query_states": q})`` followed by
+``compacted_paged_sdpa`` -- the decode-step protocol of the reference's benchmark loop
+(razorkv/evaluation/benchmark_runner.py:259-281) with the query passed in ``cache_kwargs``
+(razorkv/cache.py:392-393) -- and records what the reference produced:
+
+* ``ids_<l>``/``ids_off_<l>``: the retained token ids of layer l after every step
+  (prefill = step -1), recovered by matching retained key rows to the rows that were fed in;
+* ``out``: the attention output of every decode step (fp32);
+* ``sal_<l>``: the final salience of layer l (fp32);
+* ``input_sha``: a digest of every input tensor, so tests can check that regeneration
+  reproduces the exact inputs.
+
+The fixtures are read by tests/test_oracle_golden.py (oracle vs reference, CPU) and by
+tests/test_gpu_golden.py (CUDA path vs reference, GPU).
+"""
+
+import hashlib
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.abspath(os.path.join(HERE, "..", "..")))
+
+from tests.golden.cases import CASES, iter_inputs  # noqa: E402
+
+
+def row_key(x: torch.Tensor) -> bytes:
+    return x.float().contiguous().numpy().tobytes()
+
+
+def run_reference_case(name, case, ref_root):
+    sys.path.insert(0, ref_root)
+    from razorkv.cache import RazorKVCache
+    from razorkv.config import RazorConfig
+    from razorkv.kernels.torch_sparse import compacted_paged_sdpa
+
+    w = case["workload"]
+    cfg = RazorConfig(**case["razor"])
+    cache = RazorKVCache(config=cfg, num_layers=w.num_layers)
+    L = w.num_layers
+    rows = [dict() for _ in range(L)]
+    next_id = [0] * L
+    ids_hist = [[] for _ in range(L)]
+    outs = []
+    sha = hashlib.sha256()
+
+    def register(layer, k):
+        # k [B, Hkv, T, D]: identify tokens by their (b=0, h=0) key row
+        for t in range(k.shape[2]):
+            key = row_key(k[0, 0, t])
+            assert key not in rows[layer], "duplicate key row in workload"
+            rows[layer][key] = next_id[layer]
+            next_id[layer] += 1
+
+    def retained(layer):
+        K = cache.key_cache[layer]
+        return np.array([rows[layer][row_key(K[0, 0, t])] for t in range(K.shape[2])], np.int64)
+
+    for kind, step, layer, tensors in iter_inputs(case):
+        for t in tensors:
+            sha.update(t.float().contiguous().numpy().tobytes())
+        if kind == "prefill":
+            K, V, q0 = tensors
+            register(layer, K)
+            kw = {"query_states": q0} if case["query"] else None
+            cache.update(K, V, layer, kw)
+            ids_hist[layer].append(retained(layer))
+        else:
+            q, k, v = tensors
+            register(layer, k)
+            kw = {"query_states": q} if case["query"] else None
+            Kc, Vc = cache.update(k, v, layer, kw)
+            out = compacted_paged_sdpa(q, Kc, Vc)
+            outs.append(out.float()[:, :, 0, :].numpy())
+            ids_hist[layer].append(retained(layer))
+
+    arrays = {"input_sha": np.frombuffer(sha.digest(), np.uint8), "out": np.stack(outs)}
+    for l in range(L):
+        arrays[f"ids_{l}"] = np.concatenate(ids_hist[l])
+        arrays[f"ids_off_{l}"] = np.cumsum([0] + [len(a) for a in ids_hist[l]]).astype(np.int64)
+        arrays[f"sal_{l}"] = cache.salience_scores[l].float().numpy()
+    np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **arrays)
+    print(f"{name}: {len(outs)} steps, final lengths",
+          [cache.key_cache[l].shape[2] for l in range(L)])
+
+
+def main():
+    ref_root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("RAZORKV_REFERENCE", "")
+    if not ref_root or not os.path.isdir(os.path.join(ref_root, "razorkv")):
+        raise SystemExit("pass the path of the reference project (the directory holding razorkv/)")
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    only = sys.argv[2:] or list(CASES)
+    for name in only:
+        run_reference_case(name, CASES[name], ref_root)
+
+
+if __name__ == "__main__":
+    main()
