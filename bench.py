@@ -1,0 +1,469 @@
+#!/usr/bin/env python
+"""Decode throughput of the RazorKV sparse decode path (score + select + compact + attend).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+    python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...
+
+Workload (default): the Llama-3.1-8B-shaped cache -- 32 layers, 32 query / 8 KV heads,
+head_dim 128, bf16, batch 8 per GPU, 32768-token prefill in 16-token pages, sink 32,
+window 512, linear layer pyramid 15 % -> 70 %, 1 % planted query-aligned pages, seeded
+synthetic N(0, 1) data.  A *step* is one decode step of all layers for the whole batch:
+per layer, append the new token, score every retained token, compact when the hysteresis
+threshold is crossed, and attend over the retained pages.  Tokens/s = batch / step time.
+
+* ``value``   : device time (CUDA events, max over ranks) of K steps with inputs resident
+                in HBM; the retained KV read per step (~14.6 GB) exceeds the 126 MB L2.
+* ``e2e``     : the same steps driven through the public ``PagedRazorKVCache.decode_step``
+                with every step's q / k / v copied from pinned host memory and the step's
+                outputs copied back, inside the timed region.
+* ``roofline``: the decode kernel's algorithmic bytes (retained K + V of each launch) over
+                its CUDA-event duration, against the measured HBM copy bandwidth.
+* ``cpu_baseline`` : the CPU oracle (a restatement of the reference algorithm) timed on a
+                bounded sample of the same workload on this host's cores.
+* ``--impl reference``: the reference algorithm's CPU path (the oracle port; the reference
+                itself is Python and is not installed here) on the host cores, same metric.
+
+Multi-GPU: one process per GPU, weak scaling (batch 8 per GPU, different sequences per
+rank).  Page selection averages page scores over the global batch, so on compaction steps
+the ranks all-gather their [B_local, pages] scores (NCCL) before the identical top-k.
+"""
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode attention tokens/s/GPU and HBM GB/s (% of peak) at 32k ctx; 1/2/4/8 GPU"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=4)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--workload", default="llama8b-b8-32k-bf16")
+    ap.add_argument("--e2e-steps", type=int, default=32)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0, help="run only the first L layers (profiling)")
+    ap.add_argument("--context", type=int, default=0, help="override the prefill length (profiling)")
+    return ap.parse_args()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        sm, mx, reasons = [], 0.0, set()
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9 or not parts[0].isdigit() or int(parts[0]) != self.gpu:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx = max(mx, float(parts[2]))
+                except ValueError:
+                    continue
+                names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower().startswith("active"):
+                        reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------- helpers
+def pool_slots(w, cfg, steps):
+    P = w.page_size
+    T_end = w.context + steps + 1
+    slots = 0
+    for l in range(w.num_layers):
+        b = cfg.get_layer_budget(l, w.num_layers, T_end)
+        slots += (b + 2 * P) // P + 2
+    return slots + (w.context + P - 1) // P + 64
+
+
+class KernelTimer:
+    """CUDA events around every decode-kernel launch of decode_step."""
+
+    def __init__(self, torch):
+        self.torch = torch
+        self.pairs = []
+        self.enabled = False
+
+    def before(self, layer, kv_bytes):
+        if not self.enabled:
+            return
+        e0 = self.torch.cuda.Event(enable_timing=True)
+        e0.record()
+        self.pairs.append([e0, None, kv_bytes])
+
+    def after(self):
+        if not self.enabled:
+            return
+        e1 = self.torch.cuda.Event(enable_timing=True)
+        e1.record()
+        self.pairs[-1][1] = e1
+
+    def summary(self):
+        ms = sum(a.elapsed_time(b) for a, b, _ in self.pairs)
+        nbytes = sum(n for _, _, n in self.pairs)
+        return len(self.pairs), ms, nbytes
+
+
+def traffic_per_byte():
+    """DRAM bytes per algorithmic byte of the decode kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "decode_kernel_llama8b_layer.md")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.startswith("dram_bytes_per_algorithmic_byte:"):
+                    return float(line.split(":")[1])
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------------------- CPU oracle arm
+def oracle_sample(w, steps, warmup=0, threads=None):
+    """Time the CPU oracle (reference algorithm) on a bounded sample of workload w.
+
+    Sample: the shallowest and deepest layers (0 and L-1) at the full batch after a full
+    prefill; every decode step runs update(k, v, l, q) + attention on those two layers.
+    A full step's time is extrapolated by retained tokens: sum over all layers of the
+    layer's retained tokens times the measured seconds per retained token."""
+    import numpy as np
+    import torch
+    from oracle import razorkv_oracle as O
+    from razorkv_b200.workload import decode_inputs, layer_prefill
+
+    if threads:
+        os.environ["ORACLE_THREADS"] = str(threads)
+    O.lib()
+    cores = int(os.environ.get("ORACLE_THREADS", os.cpu_count() or 1))
+    cfg = w.razor_config()
+    ocfg = O.OracleConfig(compression_ratio=cfg.compression_ratio, sink_tokens=cfg.sink_tokens,
+                          local_window=cfg.local_window, page_size=cfg.page_size,
+                          pyramid_mode=cfg.pyramid_mode, pyramid_min_ratio=cfg.pyramid_min_ratio,
+                          pyramid_max_ratio=cfg.pyramid_max_ratio)
+    L = w.num_layers
+    layers = sorted({0, L - 1})
+    elt = torch.tensor([], dtype=w.dtype).element_size()
+    cache = O.OracleCache(ocfg, L, elt)
+    for l in layers:
+        K, V, q0 = layer_prefill(w, l, "cpu")
+        cache.update(K.float().numpy(), V.float().numpy(), l, q0.float().numpy())
+        del K, V
+    tot_time, tot_tokens, step_times = 0.0, 0, []
+    for step in range(warmup + steps):
+        t_step, n_step = 0.0, 0
+        for l in layers:
+            q, k, v = decode_inputs(w, step, l, "cpu")
+            qn, kn, vn = q.float().numpy(), k.float().numpy(), v.float().numpy()
+            t0 = time.perf_counter()
+            Kc, Vc = cache.update(kn, vn, l, qn)
+            O.attention(qn, Kc, Vc)
+            t_step += time.perf_counter() - t0
+            n_step += Kc.shape[2]
+        if step >= warmup:
+            tot_time += t_step
+            tot_tokens += n_step
+            step_times.append(t_step / n_step)
+    sec_per_token = tot_time / max(tot_tokens, 1)
+    # retained tokens of every layer at this point of the decode (budget of the final length)
+    T = cache.seen
+    retained = sum(ocfg.budget(l, L, T) for l in range(L))
+    est_step = sec_per_token * retained
+    return {
+        "value": w.batch / est_step,
+        "unit": "tokens/s",
+        "cores": cores,
+        "kind": "port",
+        "sample": (f"layers {layers} of {L}, batch {w.batch}, {w.context}-token prefill, "
+                   f"{steps} timed decode steps; full-step time extrapolated by retained tokens "
+                   f"({retained} over {L} layers)"),
+        "ms_per_step_est": est_step * 1e3,
+        "sampled_seconds": tot_time,
+    }
+
+
+def run_reference(args):
+    import torch
+    from razorkv_b200.workload import WORKLOADS
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    w = WORKLOADS[args.workload]
+    if args.context:
+        w = w.scaled(context=args.context)
+    steps = max(1, min(args.steps, 4))
+    warm = min(args.warmup, 1)
+    res = oracle_sample(w, steps, warm, threads=os.cpu_count())
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": res["value"],
+        "unit": "tokens/s",
+        "n_gpus": args.gpus,
+        "steps": steps,
+        "warmup": warm,
+        "ms_per_step": res["ms_per_step_est"],
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16" if w.dtype == torch.bfloat16 else "fp32",
+        "data": "synthetic: seeded N(0,1) K/V/q with planted query-aligned pages",
+        "config": workload_config(w, args.gpus),
+        "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": res["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config(w, n):
+    return {
+        "workload": w.name, "layers": w.num_layers, "q_heads": w.num_q_heads,
+        "kv_heads": w.num_kv_heads, "head_dim": w.head_dim, "batch_per_gpu": w.batch,
+        "global_batch": w.batch * n, "context": w.context, "page_size": w.page_size,
+        "sink": w.sink_tokens, "window": w.local_window,
+        "pyramid": f"{w.pyramid_mode} {w.pyramid_min_ratio}->{w.pyramid_max_ratio}",
+        "parallelism": f"batch-sharded x{n}" if n > 1 else "single GPU",
+        "l2": "inputs larger than L2 (retained KV per step >> 126 MB)",
+    }
+
+
+# ---------------------------------------------------------------------------- GPU arm
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+
+    from razorkv_b200 import PagedRazorKVCache, _lib
+    from razorkv_b200.workload import WORKLOADS, decode_inputs, layer_prefill
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    w = WORKLOADS[args.workload]
+    if args.context:
+        w = w.scaled(context=args.context)
+    if args.layers:
+        w = w.scaled(num_layers=args.layers)
+    # each rank holds its own sequences (weak scaling): a distinct seed per rank
+    wr = w.scaled(seed=w.seed + 1000 * rank)
+    cfg = w.razor_config()
+    L, B = w.num_layers, w.batch
+    total_steps = args.warmup + args.steps + args.e2e_steps
+    cache = PagedRazorKVCache(cfg, L, max_slots=pool_slots(w, cfg, total_steps))
+
+    if world > 1:
+        def reducer(scores):
+            out = torch.empty((world * scores.shape[0], scores.shape[1]), dtype=scores.dtype,
+                              device=scores.device)
+            dist.all_gather_into_tensor(out, scores.contiguous())
+            return out
+        cache.score_reducer = reducer
+
+    # ---- prefill (untimed)
+    t0 = time.time()
+    for l in range(L):
+        K, V, q0 = layer_prefill(wr, l, dev)
+        cache.update(K, V, l, {"query_states": q0})
+        del K, V, q0
+    torch.cuda.synchronize()
+    prefill_s = time.time() - t0
+
+    # ---- decode inputs for every step, resident in HBM
+    n_dev_steps = args.warmup + args.steps
+    inputs = [[decode_inputs(wr, s, l, dev) for l in range(L)] for s in range(n_dev_steps)]
+    outs = [torch.empty(B, w.num_q_heads, 1, w.head_dim, dtype=w.dtype, device=dev) for _ in range(L)]
+    timer = KernelTimer(torch)
+    cache.launch_observer = timer
+
+    def step(s):
+        for l in range(L):
+            q, k, v = inputs[s][l]
+            cache.decode_step(q, k, v, l, out=outs[l])
+
+    for s in range(args.warmup):
+        step(s)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    lib = _lib.load()
+    clocks = ClockSampler(local) if rank == 0 else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.4)
+    timer.enabled = True
+    launches0 = lib.rkv_launch_count()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for s in range(args.warmup, n_dev_steps):
+        step(s)
+    ev1.record()
+    torch.cuda.synchronize()
+    launches = lib.rkv_launch_count() - launches0
+    timer.enabled = False
+    clock_info = clocks.stop() if clocks else None
+    ms = ev0.elapsed_time(ev1)
+    n_launch, kern_ms, kern_bytes = timer.summary()
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+
+    # ---- end to end: host inputs, public API, outputs back to the host
+    e2e = None
+    if args.e2e_steps > 0:
+        Hq, Hkv, D = w.num_q_heads, w.num_kv_heads, w.head_dim
+        per_layer = B * (Hq + 2 * Hkv) * D
+        host_in = []
+        for s in range(n_dev_steps, total_steps):
+            buf = torch.empty(L, per_layer, dtype=w.dtype).pin_memory()
+            for l in range(L):
+                q, k, v = decode_inputs(wr, s, l, "cpu")
+                buf[l] = torch.cat([q.reshape(-1), k.reshape(-1), v.reshape(-1)])
+            host_in.append(buf)
+        host_out = torch.empty(L, B, Hq, 1, D, dtype=w.dtype).pin_memory()
+        dev_in = torch.empty(L, per_layer, dtype=w.dtype, device=dev)
+        dev_out = torch.empty(L, B, Hq, 1, D, dtype=w.dtype, device=dev)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for buf in host_in:
+            dev_in.copy_(buf, non_blocking=True)
+            for l in range(L):
+                x = dev_in[l]
+                q = x[: B * Hq * D].view(B, Hq, 1, D)
+                k = x[B * Hq * D: B * (Hq + Hkv) * D].view(B, Hkv, 1, D)
+                v = x[B * (Hq + Hkv) * D:].view(B, Hkv, 1, D)
+                cache.decode_step(q, k, v, l, out=dev_out[l])
+            host_out.copy_(dev_out, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        e_ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([e_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e_ms = float(t.item())
+        elt = torch.tensor([], dtype=w.dtype).element_size()
+        e2e = {"value": world * B * args.e2e_steps / (e_ms / 1e3), "unit": "tokens/s",
+               "steps": args.e2e_steps, "ms_per_step": e_ms / args.e2e_steps,
+               "h2d_bytes_per_step": L * per_layer * elt,
+               "d2h_bytes_per_step": L * B * Hq * D * elt}
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+
+    peak, peak_kind = peaks()
+    achieved = (kern_bytes / n_launch) / ((kern_ms / n_launch) / 1e3) / 1e9 if n_launch else 0.0
+    tpb = traffic_per_byte()
+    step_bytes = kern_bytes / max(args.steps, 1)
+    value = world * B * args.steps / (ms / 1e3)
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16" if w.dtype == torch.bfloat16 else "fp32",
+        "data": "synthetic: seeded N(0,1) K/V/q, 1% planted query-aligned pages per head",
+        "config": workload_config(w, world),
+        "impl": "b200",
+        "tokens_per_s_per_gpu": value / world,
+        "retained_kv_gb_per_step": step_bytes / 1e9,
+        "step_hbm_gbs": step_bytes / (ms / args.steps / 1e3) / 1e9,
+        "roofline": {
+            "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+            "frac": achieved / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+            "kernel": "rkv::sm100::decode_kernel (score+attend, and attend-only on compaction steps)",
+            "launches": n_launch, "kernel_ms_total": kern_ms,
+            "traffic": (tpb * kern_bytes / n_launch) if (tpb and n_launch) else None,
+        },
+        "gpu_launches": int(launches),
+        "prefill_s": prefill_s,
+        "e2e": e2e,
+        "clocks": clock_info,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        try:
+            res = oracle_sample(w, steps=2, warmup=0, threads=os.cpu_count())
+            line["cpu_baseline"] = {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        except Exception as exc:  # report, never hide
+            line["cpu_baseline"] = {"error": repr(exc)}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -107,6 +107,20 @@ typedef struct rkv_salience {
 const char* rkv_status_string(int status);
 int rkv_abi_version(void);
 
+/* Number of kernels this library has launched in this process (all threads, all devices);
+ * lets a caller count the launches inside a timed region. */
+unsigned long long rkv_launch_count(void);
+
+/* Every workspace passed to this library must start with RKV_WORKSPACE_HEADER_BYTES of
+ * zeros before its first use.  The decode kernels keep their cross-CTA merge counters and
+ * an error flag there and leave the counters at zero when each launch completes; all other
+ * workspace use starts after the header.  The *_workspace_size queries include the header. */
+#define RKV_WORKSPACE_HEADER_BYTES 65536
+
+/* Reads nothing on the device: returns the byte offset, inside a workspace, of the int32
+ * flag the decode kernels set when a bounded wait gives up (0 = no error). */
+size_t rkv_workspace_error_flag_offset(void);
+
 /* ---- attention --------------------------------------------------------------------------
  * out = softmax(q.k * scale) . v over the num_tokens tokens of each (b, kv-head), GQA head
  * h reading kv head h / (Hq/Hkv).  causal != 0 masks key t > query row (upper-left aligned).

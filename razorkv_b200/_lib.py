@@ -59,6 +59,8 @@ P = ctypes.POINTER
 _SIGNATURES = {
     "rkv_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "rkv_abi_version": (ctypes.c_int, []),
+    "rkv_launch_count": (ctypes.c_ulonglong, []),
+    "rkv_workspace_error_flag_offset": (c_sz, []),
     "rkv_decode_attention_workspace_size": (c_sz, [P(Query), P(KVLayout)]),
     "rkv_decode_attention": (ctypes.c_int, [P(Query), P(KVLayout), c_f32, ctypes.c_int,
                                             P(Output), c_vp, c_sz, c_vp]),

@@ -142,7 +142,9 @@ class PagedRazorKVCache(BaseCacheClass):
         self.record_margins = False
         self.margins: List[Tuple[int, torch.Tensor]] = []
         self.return_views = False
-        self._sel_ws = None
+        # optional observer with before(layer, kv_bytes) / after() around every attention
+        # launch of decode_step (used to time the decode kernel inside a running step)
+        self.launch_observer = None
 
     # ---------------------------------------------------------------- HF / reference surface
     @property
@@ -502,22 +504,36 @@ class PagedRazorKVCache(BaseCacheClass):
         os_ = Output(out.data_ptr(), dtype_code(out.dtype), 0, out.stride(0), out.stride(1),
                      out.stride(2))
         scale = float(scaling) if scaling else 0.0
+        obs = self.launch_observer
         if cur > budget + self.config.page_size:
             self.update_salience_with_query(q, layer_idx)
             self._evict_layer(layer_idx, budget)
             lay = self._layout(layer_idx)
             ws = Workspace.get(self._device, lib.rkv_decode_attention_workspace_size(qs, lay))
+            if obs is not None:
+                obs.before(layer_idx, self._kv_bytes(layer_idx))
             st = lib.rkv_decode_attention(qs, lay, scale, 0, os_, ws.data_ptr(), ws.numel(),
                                           self._stream())
+            if obs is not None:
+                obs.after()
             check(st, "rkv_decode_attention")
         else:
             lay = self._layout(layer_idx)
             decay = self.config.salience_decay
             ws = Workspace.get(self._device, lib.rkv_decode_fused_workspace_size(qs, lay))
+            if obs is not None:
+                obs.before(layer_idx, self._kv_bytes(layer_idx))
             st = lib.rkv_decode_fused(qs, lay, self._salience(), float(decay), float(1.0 - decay),
                                       scale, os_, ws.data_ptr(), ws.numel(), self._stream())
+            if obs is not None:
+                obs.after()
             check(st, "rkv_decode_fused")
         return out
+
+    def _kv_bytes(self, layer_idx: int) -> int:
+        """Bytes of retained K and V one attention pass over the layer reads."""
+        elt = torch.tensor([], dtype=self._dtype).element_size()
+        return 2 * self._B * self._Hkv * self._n[layer_idx] * self._D * elt
 
     def attention(self, query_states: torch.Tensor, layer_idx: int,
                   scaling: Optional[float] = None, is_causal: bool = False) -> torch.Tensor:

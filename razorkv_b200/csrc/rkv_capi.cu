@@ -2,11 +2,18 @@
 // Every function returns an rkv_status and never allocates, frees or synchronises.
 #include <math.h>
 
+#include <atomic>
+
 #include "../../include/razorkv_b200.h"
 #include "rkv_common.cuh"
 #include "rkv_kernels.h"
 
 using namespace rkv;
+
+namespace rkv {
+static std::atomic<unsigned long long> g_launches{0};
+void count_launches(int n) { g_launches.fetch_add((unsigned long long)n, std::memory_order_relaxed); }
+}  // namespace rkv
 
 namespace {
 
@@ -19,6 +26,15 @@ inline int status_of(cudaError_t e) {
 }
 
 inline bool dtype_ok(int d) { return d == RKV_F32 || d == RKV_F16 || d == RKV_BF16; }
+
+// Workspace layout: [0, 4) error flag, [256, header) per-sequence merge counters (int32),
+// [header, ...) scratch of the call.
+inline int* ws_err(void* ws) { return static_cast<int*>(ws); }
+inline int* ws_counters(void* ws) { return reinterpret_cast<int*>(static_cast<char*>(ws) + 256); }
+inline float* ws_body(void* ws) {
+    return reinterpret_cast<float*>(static_cast<char*>(ws) + RKV_WORKSPACE_HEADER_BYTES);
+}
+constexpr int64_t kMaxCounters = (RKV_WORKSPACE_HEADER_BYTES - 256) / 4;
 
 int check_kv(const rkv_kv_layout* kv, bool need_v) {
     if (!kv || !kv->k || (need_v && !kv->v)) return RKV_ERR_INVALID_ARGUMENT;
@@ -71,7 +87,7 @@ FusedParams fused_params(const rkv_query* q, const rkv_kv_layout* kv, const rkv_
     FusedParams p{};
     p.q = q->q; p.q_stride_b = q->stride_b; p.q_stride_h = q->stride_h;
     p.Hq = q->num_heads; p.Hkv = (int)kv->num_kv_heads; p.D = kv->head_dim;
-    p.B = kv->batch; p.N = kv->num_tokens;
+    p.dtype = kv->dtype; p.B = kv->batch; p.N = kv->num_tokens;
     p.k = kv->k; p.v = kv->v;
     p.stride_b = kv->stride_b; p.stride_h = kv->stride_h; p.stride_p = kv->stride_p;
     p.stride_t = kv->stride_t; p.num_slots = kv->num_slots;
@@ -107,14 +123,16 @@ const char* rkv_status_string(int s) {
 
 int rkv_abi_version(void) { return 1; }
 
+unsigned long long rkv_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
 size_t rkv_decode_attention_workspace_size(const rkv_query* q, const rkv_kv_layout* kv) {
     if (!q || !kv) return 0;
     const int64_t G = q->num_heads / (kv->num_kv_heads > 0 ? kv->num_kv_heads : 1);
     int splits = attn_num_splits(kv->num_tokens, kv->batch, kv->num_kv_heads, G * q->q_len);
     size_t generic = attn_workspace_floats(kv->batch, q->num_heads, q->q_len, kv->head_dim, splits) *
                      sizeof(float);
-    size_t fast = fused_workspace_bytes(kv->batch, q->num_heads, kv->head_dim);
-    return generic > fast ? generic : fast;
+    size_t fast = fused_workspace_bytes(kv->batch, q->num_heads, (int)kv->num_kv_heads, kv->head_dim, kv->num_tokens);
+    return RKV_WORKSPACE_HEADER_BYTES + (generic > fast ? generic : fast);
 }
 
 int rkv_decode_attention(const rkv_query* q, const rkv_kv_layout* kv, float scale, int causal,
@@ -129,13 +147,13 @@ int rkv_decode_attention(const rkv_query* q, const rkv_kv_layout* kv, float scal
         return RKV_ERR_WORKSPACE_TOO_SMALL;
     if (!causal && kv->num_tokens > 0 && fast_ok(q, kv, true)) {
         FusedParams p = fused_params(q, kv, nullptr, 0.f, 0.f, scale, out);
-        p.partials = static_cast<float*>(workspace);
+        p.partials = ws_body(workspace); p.counters = ws_counters(workspace); p.err = ws_err(workspace);
         return status_of(launch_fused(p, S(stream)));
     }
     AttnParams p = attn_params(q, kv, scale, causal, out);
     const int64_t G = q->num_heads / kv->num_kv_heads;
     p.num_splits = attn_num_splits(kv->num_tokens, kv->batch, kv->num_kv_heads, G * q->q_len);
-    p.workspace = static_cast<float*>(workspace);
+    p.workspace = ws_body(workspace);
     return status_of(launch_attention(p, S(stream)));
 }
 
@@ -218,7 +236,7 @@ int rkv_decode_fused(const rkv_query* q, const rkv_kv_layout* kv, const rkv_sali
         return RKV_ERR_WORKSPACE_TOO_SMALL;
     if (kv->num_tokens > 0 && fast_ok(q, kv, true)) {
         FusedParams p = fused_params(q, kv, sal, decay, one_minus_decay, scale, out);
-        p.partials = static_cast<float*>(workspace);
+        p.partials = ws_body(workspace); p.counters = ws_counters(workspace); p.err = ws_err(workspace);
         return status_of(launch_fused(p, S(stream)));
     }
     // shapes outside the fused kernel: the two shape-general kernels back to back
@@ -240,8 +258,10 @@ int rkv_page_scores(const rkv_kv_layout* kv, const rkv_salience* sal, int64_t fi
 }
 
 size_t rkv_select_pages_workspace_size(int64_t num_pages) {
-    return (size_t)(num_pages > 0 ? num_pages : 1) * sizeof(uint32_t);
+    return RKV_WORKSPACE_HEADER_BYTES + (size_t)(num_pages > 0 ? num_pages : 1) * sizeof(uint32_t);
 }
+
+size_t rkv_workspace_error_flag_offset(void) { return 0; }
 
 int rkv_select_pages(const float* scores, int64_t batch, int64_t num_pages, int64_t k,
                      int64_t* kept, float* margin, void* workspace, size_t workspace_bytes,
@@ -251,7 +271,7 @@ int rkv_select_pages(const float* scores, int64_t batch, int64_t num_pages, int6
     if (!workspace || workspace_bytes < rkv_select_pages_workspace_size(num_pages))
         return RKV_ERR_WORKSPACE_TOO_SMALL;
     return status_of(launch_select(scores, batch, num_pages, k, kept, margin,
-                                   static_cast<uint32_t*>(workspace), S(stream)));
+                                   reinterpret_cast<uint32_t*>(ws_body(workspace)), S(stream)));
 }
 
 int rkv_compact_pages(int64_t* page_table, int64_t sink_pages, int64_t num_pages,

@@ -1,17 +1,621 @@
-// sm_100a decode kernel (score + split-K attention over TMA-staged pages).
-// Placeholder until the specialised kernel lands: reports every shape as unsupported so the
-// shape-general kernels serve all calls.
+// sm_100a decode kernel: salience scoring and split-K paged attention in one pass over K.
+//
+// Work decomposition (stream-K over pages).  A *tile* is one 16-token page of one sequence
+// across all kv heads.  The B * ceil(N/16) tiles, sequence-major, are cut into equal
+// contiguous ranges, one per CTA (at most one CTA per SM, so every SM streams the same
+// number of bytes whatever B and N are).  A range that crosses a sequence boundary is
+// processed as one *segment* per sequence.
+//
+// CTA = 8 compute warps + 1 producer warp.
+//   producer : one lane walks the CTA's tiles, reads the page table and issues 5-D TMA tile
+//              loads (128-byte swizzle, no multicast) of K and V for all kv heads of up to
+//              8/Hkv tiles per pipeline stage into an NS-deep shared-memory ring.
+//   compute  : warp w serves kv head h = w % Hkv of tile slot s = w / Hkv of every stage,
+//              i.e. GQA packing: each K/V page is read from HBM once and used by the G query
+//              heads of its kv head.
+//
+// Per tile a compute warp
+//   1. computes the 16 x G scores q.k in fp32 on CUDA cores in the canonical order shared
+//      with the CPU oracle (lane j of an 8-lane group owns the 16-byte chunks j, j+8 of the K
+//      row; fused multiply-adds from +0.0f; xor-4/2/1 butterfly), so salience is bit-exact;
+//   2. (score) takes the max over its heads per token and folds it into the per-tile
+//      shared-memory maximum; the last of the Hkv warps of the tile applies
+//      S = fl(fl(d*S) + fl((1-d)*R)) to the 16 tokens' salience in HBM;
+//   3. (attend) runs the online softmax in the log2 domain with warp shuffles, stores the
+//      probabilities as bf16/fp16 and accumulates P.V with mma.sync m16n8k16 (Vt as the A
+//      operand straight from the swizzled stage via ldmatrix.trans, P^T as B).
+// At the end of a segment every warp writes its (m, l, acc) partial; the last CTA to finish
+// a sequence (atomic ticket, no waiting) merges the partials by log-sum-exp and writes the
+// output.  Tokens past N in the last page are masked and their V rows zeroed.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <math.h>
+
+#include <mutex>
+#include <type_traits>
+
+#include "rkv_common.cuh"
 #include "rkv_kernels.h"
+#include "rkv_sm100.cuh"
 
 namespace rkv {
+namespace sm100 {
 
-bool fused_supported(int, int, int, int, int64_t, int64_t, int64_t, int64_t, int64_t,
-                     const void*, const void*) {
-    return false;
+constexpr int kComputeWarps = 8;
+constexpr int kComputeThreads = kComputeWarps * 32;
+constexpr int kThreads = kComputeThreads + 32;
+constexpr int kTileTokens = 16;
+constexpr int kMaxStages = 6;
+constexpr int kSmemBudget = 200 * 1024;   // stage ring; the rest holds barriers and scratch
+
+struct DevArgs {
+    const void* q; int64_t q_stride_b, q_stride_h;
+    int Hq, Hkv, G, wph;
+    int64_t B, N, n_tiles, total, W, maxc;
+    const int64_t* pt; int64_t pt_stride_b; int64_t num_slots;
+    float* sal; int64_t sal_stride_b, sal_stride_p;
+    float scale_r, logit_log2, decay, omd;
+    int attend, score;
+    void* out; int64_t o_stride_b, o_stride_h;
+    float* partials; int* counters; int* err;
+    int stages, stage_bytes, tile_bytes, kv_tile_bytes, half_bytes;
+    int role[3];   // tensor-map dims 2..4 in stride order: 0 = kv head, 1 = sequence, 2 = page slot
+};
+
+struct SmemTail {             // placed after the stage ring
+    uint64_t full[kMaxStages];
+    uint64_t empty[kMaxStages];
+    int32_t phys[kMaxStages][kComputeWarps];
+    uint32_t red[kMaxStages][kComputeWarps][kTileTokens];
+    int32_t redcnt[kMaxStages][kComputeWarps];
+    uint16_t ps[kComputeWarps][8][kTileTokens];   // P (bf16/fp16) per warp: [head][token]
+    float alpha[kComputeWarps][8];
+    int last;
+    int abort;
+};
+
+template <typename T>
+__device__ __forceinline__ float to_f(T x);
+template <>
+__device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
+template <>
+__device__ __forceinline__ float to_f<__half>(__half x) { return __half2float(x); }
+
+template <typename T>
+__device__ __forceinline__ T from_f(float x);
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+template <>
+__device__ __forceinline__ __half from_f<__half>(float x) { return __float2half_rn(x); }
+
+// 8 consecutive 16-bit elements of a 128-bit word -> fp32 (exact).
+template <typename T>
+__device__ __forceinline__ void unpack8(uint4 w, float* f);
+template <>
+__device__ __forceinline__ void unpack8<__nv_bfloat16>(uint4 w, float* f) {
+    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        f[2 * i] = __uint_as_float(u[i] << 16);
+        f[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
+    }
+}
+template <>
+__device__ __forceinline__ void unpack8<__half>(uint4 w, float* f) {
+    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float2 t = __half22float2(*reinterpret_cast<const __half2*>(&u[i]));
+        f[2 * i] = t.x;
+        f[2 * i + 1] = t.y;
+    }
 }
 
-size_t fused_workspace_bytes(int64_t, int, int) { return 0; }
+template <typename T>
+__device__ __forceinline__ uint16_t to_bits(float x) {
+    T v = from_f<T>(x);
+    return *reinterpret_cast<uint16_t*>(&v);
+}
 
-cudaError_t launch_fused(const FusedParams&, cudaStream_t) { return cudaErrorNotSupported; }
+// Transpose-reduce GP per-lane partials over the 8 lanes of a group in the canonical
+// xor-4 / xor-2 / xor-1 order.  Returns the full dot of head (j >> (3 - log2 GP)).
+template <int GP>
+__device__ __forceinline__ float group_transpose_reduce(float (&v)[GP], int j) {
+    int n = GP;
+#pragma unroll
+    for (int m = 4; m >= 1; m >>= 1) {
+        const bool upper = (j & m) != 0;
+        if (n >= 2) {
+#pragma unroll
+            for (int i = 0; i < GP / 2; ++i) {
+                if (i < n / 2) {
+                    const float send = upper ? v[i] : v[i + n / 2];
+                    const float keep = upper ? v[i + n / 2] : v[i];
+                    const float recv = __shfl_xor_sync(0xffffffffu, send, m);
+                    v[i] = __fadd_rn(keep, recv);
+                }
+            }
+            n >>= 1;
+        } else {
+            v[0] = __fadd_rn(v[0], __shfl_xor_sync(0xffffffffu, v[0], m));
+        }
+    }
+    return v[0];
+}
+
+template <int GP>
+__device__ __forceinline__ int head_of_lane(int j) {
+    return GP == 8 ? j : GP == 4 ? (j >> 1) : GP == 2 ? (j >> 2) : 0;
+}
+
+template <typename T, int D, int GP>
+__global__ void __launch_bounds__(kThreads, 1)
+decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+              const DevArgs a) {
+    constexpr int HALVES = D / 64;      // 128-byte swizzle boxes per row
+    constexpr int EPL = D / 8;          // K elements a lane owns per row
+    constexpr int MT = D / 16;          // 16-dim mma row tiles
+    constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~uintptr_t(1023));
+    const int NS = a.stages;
+    SmemTail& sm = *reinterpret_cast<SmemTail*>(smem + NS * a.stage_bytes);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(&sm.full[s], 1);
+            mbar_init(&sm.empty[s], kComputeWarps);
+        }
+        fence_mbar_init();
+    }
+    for (int i = threadIdx.x; i < kMaxStages * kComputeWarps * kTileTokens; i += blockDim.x)
+        (&sm.red[0][0][0])[i] = 0u;
+    for (int i = threadIdx.x; i < kMaxStages * kComputeWarps; i += blockDim.x)
+        (&sm.redcnt[0][0])[i] = 0;
+    for (int i = threadIdx.x; i < kComputeWarps * 8 * kTileTokens; i += blockDim.x)
+        (&sm.ps[0][0][0])[i] = 0;
+    for (int i = threadIdx.x; i < kComputeWarps * 8; i += blockDim.x) (&sm.alpha[0][0])[i] = 0.f;
+    if (threadIdx.x == 0) sm.abort = 0;
+    __syncthreads();
+
+    const int64_t c = blockIdx.x;
+    const int64_t r0 = c * a.W;
+    const int64_t r1 = min(a.total, r0 + a.W);
+    const int wph = a.wph;
+    const int Hkv = a.Hkv;
+
+    // ------------------------------------------------------------------- producer warp
+    if (warp == kComputeWarps) {
+        if (lane != 0) return;
+        prefetch_tensormap(&tmk);
+        if (a.attend) prefetch_tensormap(&tmv);
+        uint32_t it = 0;
+        for (int64_t pos = r0; pos < r1;) {
+            const int64_t b = pos / a.n_tiles;
+            const int64_t seg_end = min(r1, (b + 1) * a.n_tiles);
+            const int64_t tb0 = pos - b * a.n_tiles, tb1 = seg_end - b * a.n_tiles;
+            const int64_t* ptb = a.pt + b * a.pt_stride_b;
+            for (int64_t t0 = tb0; t0 < tb1; t0 += wph, ++it) {
+                const int slot = it % NS;
+                const uint32_t par = (it / NS) & 1u;
+                if (!mbar_wait(&sm.empty[slot], par ^ 1u, a.err, &sm.abort)) return;
+                const int ntile = (int)(tb1 - t0 < wph ? tb1 - t0 : wph);
+                uint8_t* st = smem + slot * a.stage_bytes;
+                for (int s = 0; s < ntile; ++s) {
+                    int64_t phys = __ldg(ptb + t0 + s);
+                    if (phys < 0 || phys >= a.num_slots) {
+                        if (a.err) atomicExch(a.err, 2);
+                        sm.phys[slot][s] = -1;
+                        phys = 0;
+                    } else {
+                        sm.phys[slot][s] = (int32_t)phys;
+                    }
+                }
+                mbar_arrive_expect_tx(&sm.full[slot], (uint32_t)(ntile * a.tile_bytes));
+                for (int s = 0; s < ntile; ++s) {
+                    const int phys = max(sm.phys[slot][s], 0);
+                    int cc[3];
+#pragma unroll
+                    for (int k = 0; k < 3; ++k)
+                        cc[k] = a.role[k] == 0 ? 0 : a.role[k] == 1 ? (int)b : phys;
+                    uint8_t* tile = st + s * a.tile_bytes;
+#pragma unroll
+                    for (int hf = 0; hf < HALVES; ++hf) {
+                        tma_load_5d(tile + hf * a.half_bytes, &tmk, &sm.full[slot], hf * 64, 0,
+                                    cc[0], cc[1], cc[2]);
+                        if (a.attend)
+                            tma_load_5d(tile + a.kv_tile_bytes + hf * a.half_bytes, &tmv,
+                                        &sm.full[slot], hf * 64, 0, cc[0], cc[1], cc[2]);
+                    }
+                }
+            }
+            pos = seg_end;
+        }
+        return;
+    }
+
+    // ------------------------------------------------------------------- compute warps
+    const int h = warp % Hkv;       // kv head
+    const int s = warp / Hkv;       // tile slot inside a stage
+    const int g = lane >> 3, j = lane & 7;
+    const int hl = head_of_lane<GP>(j);   // query head (within the group) this lane reduces to
+    const int G = a.G;
+    const bool head_writer = (j & ((8 / GP) - 1)) == 0;   // one lane per head in each group
+    const uint32_t ps_base = smem_u32(&sm.ps[warp][0][0]);
+
+    float qreg[GP][EPL];
+    float acc[MT][4];
+    uint32_t it = 0;
+    for (int64_t pos = r0; pos < r1;) {
+        const int64_t b = pos / a.n_tiles;
+        const int64_t seg_end = min(r1, (b + 1) * a.n_tiles);
+        const int64_t tb0 = pos - b * a.n_tiles, tb1 = seg_end - b * a.n_tiles;
+
+        // fl(q * scale) for this lane's K elements: chunk j of every 64-element half
+        const T* qb = static_cast<const T*>(a.q) + b * a.q_stride_b;
+#pragma unroll
+        for (int i = 0; i < GP; ++i) {
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) {
+                const int dim = (e / 8) * 64 + 8 * j + (e % 8);
+                qreg[i][e] = i < G ? __fmul_rn(to_f<T>(qb[(int64_t)(h * G + i) * a.q_stride_h + dim]),
+                                               a.scale_r)
+                                   : 0.0f;
+            }
+        }
+        float m_run = -INFINITY, l_run = 0.0f;
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[mt][e] = 0.0f;
+
+        for (int64_t t0 = tb0; t0 < tb1; t0 += wph, ++it) {
+            const int slot = it % NS;
+            const uint32_t par = (it / NS) & 1u;
+            const bool landed = mbar_wait(&sm.full[slot], par, a.err, &sm.abort);
+            const int64_t tile = t0 + s;
+            if (landed && tile < tb1) {
+                const int nv = (int)(a.N - tile * kTileTokens < kTileTokens ? a.N - tile * kTileTokens : kTileTokens);
+                uint8_t* tbase = smem + slot * a.stage_bytes + s * a.tile_bytes;
+                const uint32_t kb = smem_u32(tbase) + h * kTileTokens * 128;
+                const uint32_t vb = kb + a.kv_tile_bytes;
+
+                // ---- 1. scores, canonical order -------------------------------------
+                float sc[4];
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    const int t = 4 * r + g;
+                    float kf[EPL];
+#pragma unroll
+                    for (int hf = 0; hf < HALVES; ++hf) {
+                        const uint4 w = lds128(kb + hf * a.half_bytes + t * 128 + ((j ^ (t & 7)) << 4));
+                        unpack8<T>(w, kf + hf * 8);
+                    }
+                    float part[GP];
+#pragma unroll
+                    for (int i = 0; i < GP; ++i) {
+                        float x = 0.0f;
+#pragma unroll
+                        for (int e = 0; e < EPL; ++e) x = __fmaf_rn(qreg[i][e], kf[e], x);
+                        part[i] = x;
+                    }
+                    sc[r] = group_transpose_reduce<GP>(part, j);
+                }
+
+                // ---- 2. resonance: max over this warp's heads, folded across kv heads ----
+                if (a.score) {
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        const int t = 4 * r + g;
+                        uint32_t key = (t < nv && hl < G) ? ordered_key(sc[r]) : 0u;
+                        key = max(key, __shfl_xor_sync(0xffffffffu, key, 1));
+                        key = max(key, __shfl_xor_sync(0xffffffffu, key, 2));
+                        key = max(key, __shfl_xor_sync(0xffffffffu, key, 4));
+                        if (j == 0 && t < nv) atomicMax(&sm.red[slot][s][t], key);
+                    }
+                    __threadfence_block();
+                    __syncwarp();
+                    int last = 0;
+                    if (lane == 0) last = atomicAdd(&sm.redcnt[slot][s], 1) == Hkv - 1;
+                    last = __shfl_sync(0xffffffffu, last, 0);
+                    if (last) {
+                        __threadfence_block();
+                        if (lane < kTileTokens) {
+                            const int phys = sm.phys[slot][s];
+                            const uint32_t key = sm.red[slot][s][lane];
+                            if (lane < nv && phys >= 0) {
+                                float* sp = a.sal + (int64_t)phys * a.sal_stride_p + b * a.sal_stride_b + lane;
+                                const float R = key_to_float(key);
+                                *sp = __fadd_rn(__fmul_rn(a.decay, *sp), __fmul_rn(a.omd, R));
+                            }
+                            sm.red[slot][s][lane] = 0u;
+                        }
+                        if (lane == 0) sm.redcnt[slot][s] = 0;
+                    }
+                }
+
+                // ---- 3. online softmax + P.V on tensor cores ------------------------------
+                if (a.attend) {
+                    float z[4];
+                    float mx = -INFINITY;
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        const int t = 4 * r + g;
+                        z[r] = (t < nv && hl < G) ? sc[r] * a.logit_log2 : -INFINITY;
+                        mx = fmaxf(mx, z[r]);
+                    }
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                    const float m_new = fmaxf(m_run, mx);
+                    const bool live = m_new != -INFINITY;
+                    const float alpha = live ? ex2(m_run - m_new) : 1.0f;
+                    float psum = 0.0f;
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        const float p = live ? ex2(z[r] - m_new) : 0.0f;
+                        psum += p;
+                        if (head_writer) sm.ps[warp][hl][4 * r + g] = to_bits<T>(p);
+                    }
+                    l_run = l_run * alpha + psum;
+                    m_run = m_new;
+                    if (head_writer && g == 0) sm.alpha[warp][hl] = alpha;
+                    if (nv < kTileTokens) {
+                        // zero V rows past the last valid token (their P is 0; keep them finite)
+                        for (int i = lane; i < (kTileTokens - nv) * 8 * HALVES; i += 32) {
+                            const int row = nv + i / (8 * HALVES);
+                            const int rem = i % (8 * HALVES);
+                            const int hf = rem / 8, ch = rem % 8;
+                            sts128(vb + hf * a.half_bytes + row * 128 + (ch << 4), make_uint4(0, 0, 0, 0));
+                        }
+                        fence_proxy_async_smem();
+                    }
+                    __syncwarp();
+                    const int n0 = 2 * (lane & 3);
+                    const float al0 = sm.alpha[warp][n0], al1 = sm.alpha[warp][n0 + 1];
+#pragma unroll
+                    for (int mt = 0; mt < MT; ++mt) {
+                        acc[mt][0] *= al0; acc[mt][1] *= al1;
+                        acc[mt][2] *= al0; acc[mt][3] *= al1;
+                    }
+                    const uint32_t b0 = lds32(ps_base + ((lane >> 2) * kTileTokens + n0) * 2);
+                    const uint32_t b1 = lds32(ps_base + ((lane >> 2) * kTileTokens + n0 + 8) * 2);
+                    const int mi = lane >> 3;
+                    const int tk = (mi >> 1) * 8 + (lane & 7);
+#pragma unroll
+                    for (int mt = 0; mt < MT; ++mt) {
+                        const int cc = 2 * mt + (mi & 1);          // 8-dim chunk 0..D/8-1
+                        const int hf = cc >> 3, c8 = cc & 7;
+                        uint32_t a0, a1, a2, a3;
+                        ldsm_x4_trans(vb + hf * a.half_bytes + tk * 128 + ((c8 ^ (tk & 7)) << 4), a0, a1, a2, a3);
+                        mma_16816<kBf16>(acc[mt], a0, a1, a2, a3, b0, b1);
+                    }
+                    __syncwarp();
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.empty[slot]);
+        }
+
+        // ---- segment end: write partial, last CTA of the sequence merges -----------------
+        if (a.attend) {
+            float l_tot = l_run + __shfl_xor_sync(0xffffffffu, l_run, 8);
+            l_tot += __shfl_xor_sync(0xffffffffu, l_tot, 16);
+            const int64_t cfirst = (b * a.n_tiles) / a.W;
+            const int64_t clast = ((b + 1) * a.n_tiles - 1) / a.W;
+            const int64_t pidx = (c - cfirst) * wph + s;
+            float* part = a.partials + ((b * a.maxc * wph + pidx) * a.Hq) * (int64_t)(D + 2);
+            if (head_writer && g == 0 && hl < G) {
+                float* ph = part + (int64_t)(h * G + hl) * (D + 2);
+                ph[0] = m_run;
+                ph[1] = l_tot;
+            }
+            const int n0 = 2 * (lane & 3);
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+                const int d0 = mt * 16 + (lane >> 2);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int n = n0 + (e & 1);
+                    const int d = d0 + (e >> 1) * 8;
+                    if (n < G) part[(int64_t)(h * G + n) * (D + 2) + 2 + d] = acc[mt][e];
+                }
+            }
+            __threadfence();
+            compute_barrier(kComputeThreads);
+            if (threadIdx.x == 0) {
+                const int nparts = (int)(clast - cfirst + 1);
+                const int old = atomicAdd(&a.counters[b], 1);
+                sm.last = old == nparts - 1;
+                if (sm.last) a.counters[b] = 0;
+            }
+            compute_barrier(kComputeThreads);
+            const bool last = sm.last;
+            if (last) {
+                __threadfence();
+                const int np = (int)(clast - cfirst + 1) * wph;
+                const float* pb = a.partials + (b * a.maxc * wph) * a.Hq * (int64_t)(D + 2);
+                T* ob = static_cast<T*>(a.out) + b * a.o_stride_b;
+                for (int idx = threadIdx.x; idx < a.Hq * D; idx += kComputeThreads) {
+                    const int hq = idx / D, d = idx % D;
+                    float M = -INFINITY;
+                    for (int p = 0; p < np; ++p)
+                        M = fmaxf(M, __ldcg(pb + ((int64_t)p * a.Hq + hq) * (D + 2)));
+                    float L = 0.f, O = 0.f;
+                    for (int p = 0; p < np; ++p) {
+                        const float* ph = pb + ((int64_t)p * a.Hq + hq) * (D + 2);
+                        const float mp = __ldcg(ph);
+                        if (mp == -INFINITY) continue;
+                        const float w = ex2(mp - M);
+                        L += __ldcg(ph + 1) * w;
+                        O += __ldcg(ph + 2 + d) * w;
+                    }
+                    ob[(int64_t)hq * a.o_stride_h + d] = from_f<T>(L > 0.f ? O / L : 0.f);
+                }
+            }
+            compute_barrier(kComputeThreads);
+        }
+        pos = seg_end;
+    }
+}
+
+// ------------------------------------------------------------------------------ host side
+static int num_sms() {
+    static int cached[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (!cached[dev]) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        cached[dev] = n > 0 ? n : 148;
+    }
+    return cached[dev];
+}
+
+struct Plan {
+    int64_t n_tiles, total, W, grid, maxc;
+    int wph, stages, stage_bytes, tile_bytes, kv_tile_bytes, half_bytes, smem_bytes;
+};
+
+static Plan make_plan(int64_t B, int64_t N, int Hkv, int D, bool attend) {
+    Plan p{};
+    p.n_tiles = (N + kTileTokens - 1) / kTileTokens;
+    p.total = B * p.n_tiles;
+    const int64_t sms = num_sms();
+    const int64_t grid0 = p.total < sms ? p.total : sms;
+    p.W = grid0 > 0 ? (p.total + grid0 - 1) / grid0 : 1;
+    p.grid = p.W > 0 ? (p.total + p.W - 1) / p.W : 0;
+    p.maxc = p.n_tiles / p.W + 2;
+    p.wph = kComputeWarps / Hkv;
+    p.half_bytes = Hkv * kTileTokens * 128;
+    p.kv_tile_bytes = (D / 64) * p.half_bytes;
+    p.tile_bytes = (attend ? 2 : 1) * p.kv_tile_bytes;
+    p.stage_bytes = p.wph * p.tile_bytes;
+    p.stages = kSmemBudget / p.stage_bytes;
+    if (p.stages > kMaxStages) p.stages = kMaxStages;
+    p.smem_bytes = p.stages * p.stage_bytes + (int)sizeof(SmemTail) + 1024;
+    return p;
+}
+
+// 5-D map over one K or V storage: dims (D, 16 tokens, then kv head / sequence / page slot
+// in ascending stride order); the box covers 64 elements x 16 tokens x all kv heads, so it
+// lands in shared memory as [Hkv][16][64] whatever the storage order.  role[] reports which
+// of the three outer dims is which.
+static bool encode_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int D, int Hkv,
+                       int64_t B, int64_t slots, int64_t st_t, int64_t st_h, int64_t st_b,
+                       int64_t st_p, int role[3]) {
+    struct Dim { int64_t n, stride; int box, role; };
+    Dim outer[3] = {{Hkv, st_h, Hkv, 0}, {B, st_b, 1, 1}, {slots, st_p, 1, 2}};
+    for (int i = 0; i < 3; ++i)
+        for (int k = i + 1; k < 3; ++k)
+            if (outer[k].stride < outer[i].stride) { Dim t = outer[i]; outer[i] = outer[k]; outer[k] = t; }
+    const cuuint64_t dims[5] = {(cuuint64_t)D, (cuuint64_t)kTileTokens, (cuuint64_t)outer[0].n,
+                                (cuuint64_t)outer[1].n, (cuuint64_t)outer[2].n};
+    const cuuint64_t strides[4] = {(cuuint64_t)st_t * 2, (cuuint64_t)outer[0].stride * 2,
+                                   (cuuint64_t)outer[1].stride * 2, (cuuint64_t)outer[2].stride * 2};
+    const cuuint32_t box[5] = {64, (cuuint32_t)kTileTokens, (cuuint32_t)outer[0].box,
+                               (cuuint32_t)outer[1].box, (cuuint32_t)outer[2].box};
+    const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    for (int i = 0; i < 3; ++i) role[i] = outer[i].role;
+    CUresult r = cuTensorMapEncodeTiled(map, dt, 5, const_cast<void*>(base), dims, strides, box,
+                                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                        CU_TENSOR_MAP_SWIZZLE_128B,
+                                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+template <typename T, int D, int GP>
+static cudaError_t launch_t(const FusedParams& f, const Plan& pl, CUtensorMapDataType dt,
+                            cudaStream_t stream) {
+    CUtensorMap mk, mv;
+    int role[3];
+    if (!encode_map(&mk, f.k, dt, D, f.Hkv, f.B, f.num_slots, f.stride_t, f.stride_h, f.stride_b,
+                    f.stride_p, role))
+        return cudaErrorInvalidValue;
+    if (f.attend) {
+        if (!encode_map(&mv, f.v, dt, D, f.Hkv, f.B, f.num_slots, f.stride_t, f.stride_h,
+                        f.stride_b, f.stride_p, role))
+            return cudaErrorInvalidValue;
+    } else {
+        mv = mk;
+    }
+    auto kern = decode_kernel<T, D, GP>;
+    static std::once_flag once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(once, [&] {
+        attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        kSmemBudget + (int)sizeof(SmemTail) + 1024);
+    });
+    if (attr_err != cudaSuccess) return attr_err;
+    DevArgs a{};
+    a.q = f.q; a.q_stride_b = f.q_stride_b; a.q_stride_h = f.q_stride_h;
+    a.Hq = f.Hq; a.Hkv = f.Hkv; a.G = f.Hq / f.Hkv; a.wph = pl.wph;
+    a.B = f.B; a.N = f.N; a.n_tiles = pl.n_tiles; a.total = pl.total; a.W = pl.W; a.maxc = pl.maxc;
+    a.pt = f.page_table; a.pt_stride_b = f.pt_stride_b; a.num_slots = f.num_slots;
+    a.sal = f.sal; a.sal_stride_b = f.sal_stride_b; a.sal_stride_p = f.sal_stride_p;
+    a.scale_r = f.scale_r; a.logit_log2 = f.logit_mul * 1.4426950408889634f;
+    a.decay = f.decay; a.omd = f.one_minus_decay;
+    a.attend = f.attend; a.score = f.sal != nullptr;
+    a.out = f.out; a.o_stride_b = f.o_stride_b; a.o_stride_h = f.o_stride_h;
+    a.partials = f.partials; a.counters = f.counters; a.err = f.err;
+    a.stages = pl.stages; a.stage_bytes = pl.stage_bytes; a.tile_bytes = pl.tile_bytes;
+    a.kv_tile_bytes = pl.kv_tile_bytes; a.half_bytes = pl.half_bytes;
+    for (int i = 0; i < 3; ++i) a.role[i] = role[i];
+    kern<<<(unsigned)pl.grid, kThreads, pl.smem_bytes, stream>>>(mk, mv, a);
+    return cudaGetLastError();
+}
+
+}  // namespace sm100
+
+// ------------------------------------------------------------------------------ dispatch
+bool fused_supported(int dtype, int D, int Hkv, int Hq, int64_t page_size, int64_t stride_t,
+                     int64_t stride_h, int64_t stride_b, int64_t stride_p, const void* k,
+                     const void* v) {
+    if (dtype != RKV_BF16 && dtype != RKV_F16) return false;
+    if (D != 64 && D != 128) return false;
+    if (Hkv != 1 && Hkv != 2 && Hkv != 4 && Hkv != 8) return false;
+    if (Hq % Hkv != 0 || Hq / Hkv > 8) return false;
+    if (page_size != sm100::kTileTokens || stride_t != D) return false;
+    const int64_t strides[3] = {stride_h, stride_b, stride_p};
+    for (int64_t st : strides)
+        if (st <= 0 || (st * 2) % 16 != 0 || st * 2 >= (int64_t(1) << 40)) return false;
+    if ((reinterpret_cast<uintptr_t>(k) & 15) || (reinterpret_cast<uintptr_t>(v) & 15)) return false;
+    return true;
+}
+
+size_t fused_workspace_bytes(int64_t B, int Hq, int Hkv, int D, int64_t N) {
+    if (B <= 0 || Hkv <= 0) return 0;
+    sm100::Plan pl = sm100::make_plan(B, N, Hkv, D, true);
+    return (size_t)B * pl.maxc * pl.wph * Hq * (D + 2) * sizeof(float);
+}
+
+cudaError_t launch_fused(const FusedParams& p, cudaStream_t st) {
+    using namespace sm100;
+    if (p.B > (RKV_WORKSPACE_HEADER_BYTES - 256) / 4) return cudaErrorNotSupported;
+    if (p.attend && (!p.partials || !p.counters || !p.out)) return cudaErrorInvalidValue;
+    const int G = p.Hq / p.Hkv;
+    const Plan pl = make_plan(p.B, p.N, p.Hkv, p.D, p.attend != 0);
+    if (pl.grid == 0) return cudaSuccess;
+    cudaError_t e;
+    if (p.dtype == RKV_BF16) {
+        const auto dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+        if (p.D == 128) e = G <= 4 ? launch_t<__nv_bfloat16, 128, 4>(p, pl, dt, st)
+                                   : launch_t<__nv_bfloat16, 128, 8>(p, pl, dt, st);
+        else e = G <= 4 ? launch_t<__nv_bfloat16, 64, 4>(p, pl, dt, st)
+                        : launch_t<__nv_bfloat16, 64, 8>(p, pl, dt, st);
+    } else {
+        const auto dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+        if (p.D == 128) e = G <= 4 ? launch_t<__half, 128, 4>(p, pl, dt, st)
+                                   : launch_t<__half, 128, 8>(p, pl, dt, st);
+        else e = G <= 4 ? launch_t<__half, 64, 4>(p, pl, dt, st)
+                        : launch_t<__half, 64, 8>(p, pl, dt, st);
+    }
+    return counted(e, 1);
+}
 
 }  // namespace rkv

@@ -514,7 +514,7 @@ cudaError_t launch_score(const ScoreParams& p, cudaStream_t st) {
     dim3 grid((unsigned)((q.N + kScoreTokens - 1) / kScoreTokens), (unsigned)q.B);
     if (q.N == 0) return cudaSuccess;
     score_kernel<<<grid, kScoreThreads, q.rows_per_chunk * q.D * sizeof(float), st>>>(q);
-    return cudaGetLastError();
+    return counted(cudaGetLastError(), 1);
 }
 
 int attn_num_splits(int64_t N, int64_t B, int64_t Hkv, int64_t rows) {
@@ -537,10 +537,10 @@ cudaError_t launch_attention(const AttnParams& p, cudaStream_t st) {
     dim3 grid((unsigned)p.num_splits, (unsigned)(p.B * p.Hkv),
               (unsigned)((rows + kAttnWarps - 1) / kAttnWarps));
     attn_split_kernel<<<grid, kAttnWarps * 32, 0, st>>>(p);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = counted(cudaGetLastError(), 1);
     if (e != cudaSuccess) return e;
     merge_kernel<<<(unsigned)(p.B * p.Hq * p.QL), 128, 0, st>>>(p);
-    return cudaGetLastError();
+    return counted(cudaGetLastError(), 1);
 }
 
 cudaError_t launch_pool(const float* sal, int64_t B, int64_t S, int64_t stride_b, int64_t P,
@@ -551,20 +551,20 @@ cudaError_t launch_pool(const float* sal, int64_t B, int64_t S, int64_t stride_b
     if (total == 0) return cudaSuccess;
     pool_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(sal, B, S, stride_b, P, n_pages,
                                                                  mean, out);
-    return cudaGetLastError();
+    return counted(cudaGetLastError(), 1);
 }
 
 cudaError_t launch_page_scores(const PageScoreParams& p, cudaStream_t st) {
     if (p.num_pages == 0 || p.B == 0) return cudaSuccess;
     dim3 grid((unsigned)((p.num_pages + 255) / 256), (unsigned)p.B);
     page_scores_kernel<<<grid, 256, 0, st>>>(p);
-    return cudaGetLastError();
+    return counted(cudaGetLastError(), 1);
 }
 
 cudaError_t launch_select(const float* scores, int64_t B, int64_t n, int64_t k, int64_t* kept,
                           float* margin, uint32_t* keys, cudaStream_t st) {
     select_kernel<<<1, kSelThreads, 0, st>>>(scores, B, n, k, kept, margin, keys);
-    return cudaGetLastError();
+    return counted(cudaGetLastError(), 1);
 }
 
 cudaError_t launch_compact_pages(int64_t* pt, int64_t sink_pages, int64_t num_pages,
@@ -573,35 +573,35 @@ cudaError_t launch_compact_pages(int64_t* pt, int64_t sink_pages, int64_t num_pa
                                  cudaStream_t st) {
     compact_pages_kernel<<<1, 1024, 0, st>>>(pt, sink_pages, num_pages, kept, k, tail_first,
                                              n_total, free_stack, free_top);
-    return cudaGetLastError();
+    return counted(cudaGetLastError(), 1);
 }
 
 cudaError_t launch_append(const AppendParams& p, cudaStream_t st) {
     int64_t groups = p.n_new * p.B;
     if (groups == 0) return cudaSuccess;
     append_kernel<<<(unsigned)((groups * 8 + 255) / 256), 256, 0, st>>>(p);
-    return cudaGetLastError();
+    return counted(cudaGetLastError(), 1);
 }
 
 cudaError_t launch_compact_tokens(const CompactTokensParams& p, cudaStream_t st) {
     int64_t total = p.new_len * p.B * p.Hkv * ((p.D + 3) / 4);
     if (total == 0) return cudaSuccess;
     compact_tokens_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(p);
-    return cudaGetLastError();
+    return counted(cudaGetLastError(), 1);
 }
 
 cudaError_t launch_release(const int64_t* pages, int64_t n, int64_t* free_stack, int64_t top,
                            cudaStream_t st) {
     if (n == 0) return cudaSuccess;
     release_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(pages, n, free_stack, top);
-    return cudaGetLastError();
+    return counted(cudaGetLastError(), 1);
 }
 
 cudaError_t launch_gather(const GatherParams& p, cudaStream_t st) {
     int64_t total = p.B * p.Hkv * p.N * p.D;
     if (total == 0) return cudaSuccess;
     gather_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(p);
-    return cudaGetLastError();
+    return counted(cudaGetLastError(), 1);
 }
 
 }  // namespace rkv

@@ -7,6 +7,13 @@
 
 namespace rkv {
 
+// Library-wide count of kernel launches (reported by rkv_launch_count()).
+void count_launches(int n);
+inline cudaError_t counted(cudaError_t e, int n) {
+    if (e == cudaSuccess) count_launches(n);
+    return e;
+}
+
 struct ScoreParams {
     const void* q; int q_dtype; int64_t q_stride_b, q_stride_h, q_stride_t;
     int Hq, QL;
@@ -65,7 +72,7 @@ struct GatherParams {
 // Fused score + attention for the sm_100a fast path (rkv_decode_sm100.cu).
 struct FusedParams {
     const void* q; int64_t q_stride_b, q_stride_h;
-    int Hq, Hkv, D; int64_t B, N;
+    int Hq, Hkv, D, dtype; int64_t B, N;
     const void* k; const void* v;
     int64_t stride_b, stride_h, stride_p, stride_t, num_slots;
     const int64_t* page_table; int64_t pt_stride_b;
@@ -73,7 +80,7 @@ struct FusedParams {
     float scale_r, logit_mul, decay, one_minus_decay;
     int attend;                                        // 0: score only (no V, no output)
     void* out; int64_t o_stride_b, o_stride_h;
-    float* partials; int* counters; int grid;
+    float* partials; int* counters; int* err;   // workspace body / header (nullptr: score only)
 };
 
 cudaError_t launch_score(const ScoreParams& p, cudaStream_t st);
@@ -99,7 +106,7 @@ cudaError_t launch_gather(const GatherParams& p, cudaStream_t st);
 bool fused_supported(int dtype, int D, int Hkv, int Hq, int64_t page_size, int64_t stride_t,
                      int64_t stride_h, int64_t stride_b, int64_t stride_p, const void* k,
                      const void* v);
-size_t fused_workspace_bytes(int64_t B, int Hq, int D);
+size_t fused_workspace_bytes(int64_t B, int Hq, int Hkv, int D, int64_t N);
 cudaError_t launch_fused(const FusedParams& p, cudaStream_t st);
 
 }  // namespace rkv

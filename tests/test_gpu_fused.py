@@ -1,0 +1,130 @@
+"""The sm_100a fused decode kernel (score + attention in one pass) against the oracle (GPU).
+
+A random page pool in the cache layout [slots, B, Hkv, 16, D] with a shuffled page table is
+scored and attended through the C ABI; the salience must equal the oracle's canonical-order
+EWMA bit for bit and the output must match fp64 attention within the bf16 tolerance.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import razorkv_oracle as O
+from razorkv_b200 import _lib
+from razorkv_b200._lib import KVLayout, Output, Query, Salience, dtype_code
+from razorkv_b200.kernels import Workspace
+
+pytestmark = pytest.mark.gpu
+
+P = 16
+
+
+def _setup(B, Hq, Hkv, D, N, dtype, seed):
+    g = torch.Generator().manual_seed(seed)
+    n_pages = (N + P - 1) // P
+    slots = n_pages + 7
+    kpool = torch.randn(slots, B, Hkv, P, D, generator=g).to(dtype)
+    vpool = torch.randn(slots, B, Hkv, P, D, generator=g).to(dtype)
+    spool = (torch.rand(slots, B, P, generator=g) * 10 + 1).float()
+    pt = torch.randperm(slots, generator=g)[:n_pages].to(torch.int64)
+    q = torch.randn(B, Hq, 1, D, generator=g).to(dtype)
+    return kpool, vpool, spool, pt, q
+
+
+def _logical(pool, pt, N):
+    # [slots, B, Hkv, P, D] -> [B, Hkv, N, D] in logical token order
+    x = pool[pt].permute(1, 2, 0, 3, 4).reshape(pool.shape[1], pool.shape[2], -1, pool.shape[4])
+    return x[:, :, :N]
+
+
+def _sal_logical(spool, pt, N):
+    return spool[pt].permute(1, 0, 2).reshape(spool.shape[1], -1)[:, :N]
+
+
+def _layout(kd, vd, ptd, N):
+    return KVLayout(kd.data_ptr(), vd.data_ptr() if vd is not None else None, dtype_code(kd.dtype),
+                    kd.shape[4], kd.shape[1], kd.shape[2], kd.stride(1), kd.stride(2), kd.stride(0),
+                    kd.stride(3), P, kd.shape[0], ptd.data_ptr(), 0, N)
+
+
+SHAPES = [
+    # B, Hq, Hkv, D, N
+    (8, 32, 8, 128, 1000),     # Llama-8B-like heads, ragged last page
+    (1, 28, 4, 128, 5003),     # Qwen-like GQA 7 (padded to 8 heads per kv head)
+    (2, 64, 8, 128, 777),      # GQA 8
+    (3, 8, 2, 128, 64),        # 2 kv heads, 4 tiles per stage
+    (2, 4, 1, 128, 300),       # 1 kv head, 8 tiles per stage
+    (4, 16, 4, 64, 513),       # head_dim 64
+    (1, 8, 8, 128, 16),        # one page, G = 1
+    (5, 40, 8, 128, 3),        # fewer tokens than a page
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("B,Hq,Hkv,D,N", SHAPES)
+def test_fused_matches_oracle(B, Hq, Hkv, D, N, dtype):
+    kpool, vpool, spool, pt, q = _setup(B, Hq, Hkv, D, N, dtype, seed=B * 131 + N)
+    kd, vd, sd, ptd, qd = (t.cuda() for t in (kpool, vpool, spool, pt, q))
+    out = torch.empty_like(qd)
+    lib = _lib.load()
+    lay = _layout(kd, vd, ptd, N)
+    qs = Query(qd.data_ptr(), dtype_code(dtype), Hq, 1, qd.stride(0), qd.stride(1), qd.stride(2))
+    os_ = Output(out.data_ptr(), dtype_code(dtype), 0, out.stride(0), out.stride(1), out.stride(2))
+    sal = Salience(sd.data_ptr(), sd.stride(1), sd.stride(0))
+    ws = Workspace.get(qd.device, lib.rkv_decode_fused_workspace_size(qs, lay))
+    st = lib.rkv_decode_fused(qs, lay, sal, 0.98, 1.0 - 0.98, 0.0, os_, ws.data_ptr(), ws.numel(),
+                              torch.cuda.current_stream().cuda_stream)
+    assert st == 0
+    torch.cuda.synchronize()
+    assert int(ws[:4].view(torch.int32)[0]) == 0, "device wait gave up"
+    K = _logical(kpool, pt, N).float().numpy()
+    V = _logical(vpool, pt, N).float().numpy()
+    S0 = _sal_logical(spool, pt, N).numpy()
+    R = O.resonance(q.float().numpy(), K, 2)
+    expect_S = O.ewma(S0, R, 0.98)
+    got_S = _sal_logical(sd.cpu(), pt, N).numpy()
+    assert np.array_equal(got_S.view(np.uint32), expect_S.view(np.uint32))
+    # salience of slots outside the table is untouched
+    untouched = torch.ones(spool.shape[0], dtype=torch.bool)
+    untouched[pt] = False
+    assert torch.equal(sd.cpu()[untouched], spool[untouched])
+    ref = O.attention(q.float().numpy(), K, V)
+    np.testing.assert_allclose(out.float().cpu().numpy(), ref, atol=2e-2, rtol=1e-2)
+    # counters returned to zero
+    assert int(ws[256:256 + 4 * B].view(torch.int32).abs().sum()) == 0
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,D,N", SHAPES[:4])
+def test_fast_score_only_matches_oracle(B, Hq, Hkv, D, N):
+    kpool, vpool, spool, pt, q = _setup(B, Hq, Hkv, D, N, torch.bfloat16, seed=7 + N)
+    kd, sd, ptd, qd = (t.cuda() for t in (kpool, spool, pt, q))
+    lib = _lib.load()
+    lay = _layout(kd, None, ptd, N)
+    qs = Query(qd.data_ptr(), dtype_code(torch.bfloat16), Hq, 1, qd.stride(0), qd.stride(1), qd.stride(2))
+    sal = Salience(sd.data_ptr(), sd.stride(1), sd.stride(0))
+    st = lib.rkv_score(qs, lay, sal, 0.98, 1.0 - 0.98, 1, torch.cuda.current_stream().cuda_stream)
+    assert st == 0
+    K = _logical(kpool, pt, N).float().numpy()
+    expect_S = O.ewma(_sal_logical(spool, pt, N).numpy(), O.resonance(q.float().numpy(), K, 2), 0.98)
+    got_S = _sal_logical(sd.cpu(), pt, N).numpy()
+    assert np.array_equal(got_S.view(np.uint32), expect_S.view(np.uint32))
+
+
+def test_fused_repeated_launches_are_stable():
+    """Counters self-reset: back-to-back launches give identical outputs."""
+    B, Hq, Hkv, D, N = 8, 32, 8, 128, 4000
+    kpool, vpool, spool, pt, q = _setup(B, Hq, Hkv, D, N, torch.bfloat16, seed=99)
+    kd, vd, ptd, qd = (t.cuda() for t in (kpool, vpool, pt, q))
+    lib = _lib.load()
+    lay = _layout(kd, vd, ptd, N)
+    qs = Query(qd.data_ptr(), dtype_code(torch.bfloat16), Hq, 1, qd.stride(0), qd.stride(1), qd.stride(2))
+    outs = []
+    for _ in range(3):
+        out = torch.empty_like(qd)
+        os_ = Output(out.data_ptr(), dtype_code(torch.bfloat16), 0, out.stride(0), out.stride(1), out.stride(2))
+        ws = Workspace.get(qd.device, lib.rkv_decode_attention_workspace_size(qs, lay))
+        st = lib.rkv_decode_attention(qs, lay, 0.0, 0, os_, ws.data_ptr(), ws.numel(),
+                                      torch.cuda.current_stream().cuda_stream)
+        assert st == 0
+        outs.append(out)
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
