@@ -52,7 +52,9 @@ def parse_args():
     ap.add_argument("--workload", default="llama8b-b8-32k-bf16")
     ap.add_argument("--e2e-steps", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--layers", type=int, default=0, help="run only the first L layers (profiling)")
+    ap.add_argument("--only-layer", type=int, default=-1,
+                    help="run a single layer of the workload (budget as in the full model); "
+                         "a small case for profiling")
     ap.add_argument("--context", type=int, default=0, help="override the prefill length (profiling)")
     return ap.parse_args()
 
@@ -119,11 +121,11 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------- helpers
-def pool_slots(w, cfg, steps):
+def pool_slots(w, cfg, steps, layers):
     P = w.page_size
     T_end = w.context + steps + 1
     slots = 0
-    for l in range(w.num_layers):
+    for l in layers:
         b = cfg.get_layer_budget(l, w.num_layers, T_end)
         slots += (b + 2 * P) // P + 2
     return slots + (w.context + P - 1) // P + 64
@@ -136,20 +138,26 @@ class KernelTimer:
         self.torch = torch
         self.pairs = []
         self.enabled = False
+        self.pool = []
+
+    def prepare(self, n):
+        """Create the events up front so recording costs the host as little as possible."""
+        mk = lambda: self.torch.cuda.Event(enable_timing=True)
+        self.pool = [(mk(), mk()) for _ in range(n)]
 
     def before(self, layer, kv_bytes):
         if not self.enabled:
             return
-        e0 = self.torch.cuda.Event(enable_timing=True)
+        i = len(self.pairs)
+        e0, e1 = self.pool[i] if i < len(self.pool) else (
+            self.torch.cuda.Event(enable_timing=True), self.torch.cuda.Event(enable_timing=True))
         e0.record()
-        self.pairs.append([e0, None, kv_bytes])
+        self.pairs.append([e0, e1, kv_bytes])
 
     def after(self):
         if not self.enabled:
             return
-        e1 = self.torch.cuda.Event(enable_timing=True)
-        e1.record()
-        self.pairs[-1][1] = e1
+        self.pairs[-1][1].record()
 
     def summary(self):
         ms = sum(a.elapsed_time(b) for a, b, _ in self.pairs)
@@ -304,14 +312,13 @@ def main():
     w = WORKLOADS[args.workload]
     if args.context:
         w = w.scaled(context=args.context)
-    if args.layers:
-        w = w.scaled(num_layers=args.layers)
     # each rank holds its own sequences (weak scaling): a distinct seed per rank
     wr = w.scaled(seed=w.seed + 1000 * rank)
     cfg = w.razor_config()
     L, B = w.num_layers, w.batch
+    layers = [args.only_layer] if args.only_layer >= 0 else list(range(L))
     total_steps = args.warmup + args.steps + args.e2e_steps
-    cache = PagedRazorKVCache(cfg, L, max_slots=pool_slots(w, cfg, total_steps))
+    cache = PagedRazorKVCache(cfg, L, max_slots=pool_slots(w, cfg, total_steps, layers))
 
     if world > 1:
         def reducer(scores):
@@ -323,7 +330,7 @@ def main():
 
     # ---- prefill (untimed)
     t0 = time.time()
-    for l in range(L):
+    for l in layers:
         K, V, q0 = layer_prefill(wr, l, dev)
         cache.update(K, V, l, {"query_states": q0})
         del K, V, q0
@@ -332,13 +339,21 @@ def main():
 
     # ---- decode inputs for every step, resident in HBM
     n_dev_steps = args.warmup + args.steps
-    inputs = [[decode_inputs(wr, s, l, dev) for l in range(L)] for s in range(n_dev_steps)]
-    outs = [torch.empty(B, w.num_q_heads, 1, w.head_dim, dtype=w.dtype, device=dev) for _ in range(L)]
+    inputs = [{l: decode_inputs(wr, s, l, dev) for l in layers} for s in range(n_dev_steps)]
+    outs = {l: torch.empty(B, w.num_q_heads, 1, w.head_dim, dtype=w.dtype, device=dev) for l in layers}
     timer = KernelTimer(torch)
     cache.launch_observer = timer
 
+    single = len(layers) == 1 and layers[0] != 0
+    if single:
+        # the cache counts logical tokens on layer 0 (as the reference does); a single-layer
+        # profiling run keeps that count as the full model would
+        cache._seen_tokens = w.context
+
     def step(s):
-        for l in range(L):
+        if single:
+            cache._seen_tokens += 1
+        for l in layers:
             q, k, v = inputs[s][l]
             cache.decode_step(q, k, v, l, out=outs[l])
 
@@ -352,13 +367,16 @@ def main():
     if clocks:
         clocks.start()
         time.sleep(0.4)
+    timer.prepare(args.steps * len(layers) + 8)
     timer.enabled = True
     launches0 = lib.rkv_launch_count()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
+    h0 = time.perf_counter()
     for s in range(args.warmup, n_dev_steps):
         step(s)
+    host_ms = (time.perf_counter() - h0) * 1e3   # time to enqueue the steps (host side)
     ev1.record()
     torch.cuda.synchronize()
     launches = lib.rkv_launch_count() - launches0
@@ -378,15 +396,16 @@ def main():
         Hq, Hkv, D = w.num_q_heads, w.num_kv_heads, w.head_dim
         per_layer = B * (Hq + 2 * Hkv) * D
         host_in = []
+        nl = len(layers)
         for s in range(n_dev_steps, total_steps):
-            buf = torch.empty(L, per_layer, dtype=w.dtype).pin_memory()
-            for l in range(L):
+            buf = torch.empty(nl, per_layer, dtype=w.dtype).pin_memory()
+            for i, l in enumerate(layers):
                 q, k, v = decode_inputs(wr, s, l, "cpu")
-                buf[l] = torch.cat([q.reshape(-1), k.reshape(-1), v.reshape(-1)])
+                buf[i] = torch.cat([q.reshape(-1), k.reshape(-1), v.reshape(-1)])
             host_in.append(buf)
-        host_out = torch.empty(L, B, Hq, 1, D, dtype=w.dtype).pin_memory()
-        dev_in = torch.empty(L, per_layer, dtype=w.dtype, device=dev)
-        dev_out = torch.empty(L, B, Hq, 1, D, dtype=w.dtype, device=dev)
+        host_out = torch.empty(nl, B, Hq, 1, D, dtype=w.dtype).pin_memory()
+        dev_in = torch.empty(nl, per_layer, dtype=w.dtype, device=dev)
+        dev_out = torch.empty(nl, B, Hq, 1, D, dtype=w.dtype, device=dev)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
@@ -394,12 +413,12 @@ def main():
         e0.record()
         for buf in host_in:
             dev_in.copy_(buf, non_blocking=True)
-            for l in range(L):
-                x = dev_in[l]
+            for i, l in enumerate(layers):
+                x = dev_in[i]
                 q = x[: B * Hq * D].view(B, Hq, 1, D)
                 k = x[B * Hq * D: B * (Hq + Hkv) * D].view(B, Hkv, 1, D)
                 v = x[B * (Hq + Hkv) * D:].view(B, Hkv, 1, D)
-                cache.decode_step(q, k, v, l, out=dev_out[l])
+                cache.decode_step(q, k, v, l, out=dev_out[i])
             host_out.copy_(dev_out, non_blocking=True)
         e1.record()
         torch.cuda.synchronize()
@@ -411,8 +430,8 @@ def main():
         elt = torch.tensor([], dtype=w.dtype).element_size()
         e2e = {"value": world * B * args.e2e_steps / (e_ms / 1e3), "unit": "tokens/s",
                "steps": args.e2e_steps, "ms_per_step": e_ms / args.e2e_steps,
-               "h2d_bytes_per_step": L * per_layer * elt,
-               "d2h_bytes_per_step": L * B * Hq * D * elt}
+               "h2d_bytes_per_step": nl * per_layer * elt,
+               "d2h_bytes_per_step": nl * B * Hq * D * elt}
 
     if world > 1:
         dist.barrier()
@@ -452,6 +471,7 @@ def main():
         },
         "gpu_launches": int(launches),
         "prefill_s": prefill_s,
+        "host_enqueue_ms_per_step": host_ms / args.steps,
         "e2e": e2e,
         "clocks": clock_info,
     }

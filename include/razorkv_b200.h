@@ -162,6 +162,19 @@ int rkv_decode_fused(const rkv_query* q, const rkv_kv_layout* kv, const rkv_sali
                      float decay, float one_minus_decay, float scale, const rkv_output* out,
                      void* workspace, size_t workspace_bytes, void* stream);
 
+/* One non-compacting decode step of a layer in a single call: rkv_append of the single new
+ * token (k_new / v_new [B, Hkv, 1, D]) at position kv->num_tokens, then rkv_decode_fused over
+ * the kv->num_tokens + 1 tokens.  The caller lowers its free-stack top by one when
+ * kv->num_tokens % page_size == 0 (a page was taken).  Replaces the append half of
+ * razorkv/cache.py:361-390, the scoring call at :392-393 and the attention over the returned
+ * cache, for steps that do not cross the hysteresis threshold (:409-412). */
+int rkv_append_decode(const rkv_kv_layout* kv, const rkv_salience* sal, const void* k_new,
+                      const void* v_new, int64_t new_stride_b, int64_t new_stride_h,
+                      int64_t* page_table, const int64_t* free_stack, int64_t free_top,
+                      int salience_init, const rkv_query* q, float decay, float one_minus_decay,
+                      float scale, const rkv_output* out, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
 /* ---- cache: selection --------------------------------------------------------------------
  * scores[b, p] = max over i < sel_page_size of S(b, first_token + p*sel_page_size + i),
  * p < num_pages, written with row stride num_pages. */

@@ -18,9 +18,11 @@
  * vector_norm, mean) have ISA-dependent orders that no restatement can reproduce, so the
  * oracle and the CUDA kernels share ONE fixed order and agree bit for bit; the reference
  * differs from both by a few ulps.  A dot product over D elements of a K row whose
- * element size is E bytes is cut into 16-byte chunks of CH = 16/E elements.  Partial j
- * (j = 0..7) accumulates, with fused multiply-add starting from +0.0f, the chunks
- * c = j, j+8, j+16, ... in ascending order, elements in ascending order within a chunk.
+ * element size is E bytes is cut into 16-byte chunks of CH = 16/E elements.  Lane j
+ * (j = 0..7) owns the chunks c = j, j+8, j+16, ...; listing its elements in ascending
+ * order (chunk by chunk), the elements at even positions of that list accumulate into one
+ * chain and those at odd positions into another, each with fused multiply-add starting
+ * from +0.0f (the two halves of one packed f32x2 FMA on the GPU); partial p_j = even + odd.
  * The eight partials are combined as ((p0+p4)+(p2+p6)) + ((p1+p5)+(p3+p7)), which is the
  * xor-4 / xor-2 / xor-1 butterfly the GPU performs across eight lanes.
  *
@@ -72,12 +74,16 @@ static void parallel_for(int64_t n, range_fn fn, void *ctx) {
 static float canon_dot(const float *a, const float *b, int64_t D, int64_t ch) {
     float p[8];
     for (int j = 0; j < 8; ++j) {
-        float acc = 0.0f;
+        float even = 0.0f, odd = 0.0f;
+        int64_t pos = 0;
         for (int64_t c = j; c * ch < D; c += 8) {
             int64_t e0 = c * ch, e1 = e0 + ch < D ? e0 + ch : D;
-            for (int64_t e = e0; e < e1; ++e) acc = fmaf(a[e], b[e], acc);
+            for (int64_t e = e0; e < e1; ++e, ++pos) {
+                if (pos & 1) odd = fmaf(a[e], b[e], odd);
+                else even = fmaf(a[e], b[e], even);
+            }
         }
-        p[j] = acc;
+        p[j] = even + odd;
     }
     float s04 = p[0] + p[4], s26 = p[2] + p[6], s15 = p[1] + p[5], s37 = p[3] + p[7];
     return (s04 + s26) + (s15 + s37);

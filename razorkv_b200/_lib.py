@@ -73,6 +73,9 @@ _SIGNATURES = {
     "rkv_decode_fused_workspace_size": (c_sz, [P(Query), P(KVLayout)]),
     "rkv_decode_fused": (ctypes.c_int, [P(Query), P(KVLayout), P(Salience), c_f32, c_f32,
                                         c_f32, P(Output), c_vp, c_sz, c_vp]),
+    "rkv_append_decode": (ctypes.c_int, [P(KVLayout), P(Salience), c_vp, c_vp, c_i64, c_i64,
+                                         c_vp, c_vp, c_i64, ctypes.c_int, P(Query), c_f32, c_f32,
+                                         c_f32, P(Output), c_vp, c_sz, c_vp]),
     "rkv_page_scores": (ctypes.c_int, [P(KVLayout), P(Salience), c_i64, c_i64, c_i64, c_vp,
                                        c_vp]),
     "rkv_select_pages_workspace_size": (c_sz, [c_i64]),
@@ -130,7 +133,9 @@ def dtype_code(dt: torch.dtype) -> int:
 
 
 def stream_ptr(device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+    """Raw handle of torch's current stream on `device` (cheap: no Stream object)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    return torch._C._cuda_getCurrentRawStream(idx)
 
 
 def require_cuda(*tensors):

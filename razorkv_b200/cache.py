@@ -145,6 +145,17 @@ class PagedRazorKVCache(BaseCacheClass):
         # optional observer with before(layer, kv_bytes) / after() around every attention
         # launch of decode_step (used to time the decode kernel inside a running step)
         self.launch_observer = None
+        # argument blocks reused by the decode fast path
+        self._lib = None
+        self._ratio_cache = {}
+        self._lay_cache = {}
+        self._ws = {}
+        self._q_struct = Query()
+        self._o_struct = Output()
+        self._sal_struct = None
+        self._elt = 0
+        self._dtype_code = 0
+        self._sal_init = 0
 
     # ---------------------------------------------------------------- HF / reference surface
     @property
@@ -239,7 +250,10 @@ class PagedRazorKVCache(BaseCacheClass):
         self._B, self._Hkv, _, self._D = k.shape
         self._dtype = k.dtype
         self._device = k.device
-        dtype_code(k.dtype)
+        self._dtype_code = dtype_code(k.dtype)
+        self._elt = k.element_size()
+        self._sal_init = _lib.SAL_NORM if self.config.salience_init == "norm" else _lib.SAL_UNIFORM
+        self._lib = _lib.load()
         self._grow(self._initial_slots or 64)
 
     def _slot_shape(self, n):
@@ -269,6 +283,12 @@ class PagedRazorKVCache(BaseCacheClass):
         self._k, self._v, self._s, self._free = k, v, s, free
         self._free_top += new - old
         self._slots = new
+        self._pool_changed()
+
+    def _pool_changed(self):
+        """Pool tensors were replaced: drop argument blocks that point into them."""
+        self._lay_cache.clear()
+        self._sal_struct = self._salience()
 
     def _ensure_free(self, n_pages: int):
         if self._free_top < n_pages:
@@ -288,6 +308,7 @@ class PagedRazorKVCache(BaseCacheClass):
             if pt is not None:
                 new[: pt.numel()].copy_(pt)
             self._pt[layer_idx] = new
+            self._lay_cache.pop(layer_idx, None)
 
     def _layout(self, layer_idx: int, n_tokens: Optional[int] = None) -> KVLayout:
         k = self._k
@@ -430,6 +451,7 @@ class PagedRazorKVCache(BaseCacheClass):
         check(st, "rkv_release_pages")
         self._free_top += old_pages
         self._pt[layer_idx] = new_pt
+        self._lay_cache.pop(layer_idx, None)
         self._n[layer_idx] = new_len
 
     # ------------------------------------------------------------------------------ update
@@ -483,6 +505,10 @@ class PagedRazorKVCache(BaseCacheClass):
         razorkv/cache.py:361-414 then razorkv/kernels/torch_sparse.py:15-61).
 
         q [B, Hq, 1, D]; k, v [B, Hkv, 1, D]; returns [B, Hq, 1, D] in q's dtype."""
+        fast = self._decode_step_fast(query_states, key_states, value_states, layer_idx, out,
+                                      scaling)
+        if fast is not None:
+            return fast
         self._ensure_layer(layer_idx)
         if self._k is None:
             self._init_pool(key_states)
@@ -530,10 +556,80 @@ class PagedRazorKVCache(BaseCacheClass):
             check(st, "rkv_decode_fused")
         return out
 
+    def _decode_step_fast(self, q, k, v, layer_idx, out, scaling):
+        """The common decode step -- no compaction, no pool or table growth -- in one library
+        call with cached argument blocks.  Returns None when the step needs the general path."""
+        if self._k is None or layer_idx >= len(self._n):
+            return None
+        n0 = self._n[layer_idx]
+        if n0 is None or n0 == 0:
+            return None
+        P = self.config.page_size
+        new_page = n0 % P == 0
+        pt = self._pt[layer_idx]
+        if (new_page and (self._free_top < 1 or pt.numel() < n0 // P + 1)):
+            return None
+        if (k.dtype != self._dtype or q.dtype != self._dtype or k.shape[2] != 1
+                or k.shape[0] != self._B or k.shape[1] != self._Hkv or k.shape[3] != self._D
+                or v.shape != k.shape or k.stride() != v.stride() or k.stride(3) != 1
+                or q.stride(3) != 1 or not k.is_cuda):
+            return None
+        cur = n0 + 1
+        seen = self._seen_tokens + 1 if layer_idx == 0 else self._seen_tokens
+        T = max(seen, cur)
+        floor = self.config.sink_tokens + self.config.local_window
+        if T <= floor:
+            budget = T
+        else:
+            num_layers = max(self.num_layers, len(self._n))
+            key = (layer_idx, num_layers)
+            ratio = self._ratio_cache.get(key)
+            if ratio is None:
+                ratio = self._ratio_cache[key] = self.config.get_layer_ratio(layer_idx, num_layers)
+            budget = min(T, max(floor, int(T * ratio)))
+        if cur > budget + P:
+            return None
+        B, Hq, _, D = q.shape
+        if out is None:
+            out = torch.empty(B, Hq, 1, D, dtype=q.dtype, device=q.device)
+        lay = self._lay_cache.get(layer_idx)
+        if lay is None:
+            lay = self._lay_cache[layer_idx] = self._layout(layer_idx)
+        lay.num_tokens = n0
+        qs, os_ = self._q_struct, self._o_struct
+        qs.q = q.data_ptr(); qs.dtype = self._dtype_code; qs.num_heads = Hq; qs.q_len = 1
+        qs.stride_b = q.stride(0); qs.stride_h = q.stride(1); qs.stride_t = q.stride(2)
+        os_.out = out.data_ptr(); os_.dtype = self._dtype_code
+        os_.stride_b = out.stride(0); os_.stride_h = out.stride(1); os_.stride_t = out.stride(2)
+        lay.num_tokens = cur
+        ws_need = self._lib.rkv_decode_fused_workspace_size(qs, lay)
+        lay.num_tokens = n0
+        stream = stream_ptr(self._device)
+        ws = self._ws.get(stream)
+        if ws is None or ws.numel() < ws_need:
+            ws = self._ws[stream] = Workspace.get(self._device, ws_need)
+        decay = self.config.salience_decay
+        obs = self.launch_observer
+        if obs is not None:
+            obs.before(layer_idx, 2 * B * self._Hkv * cur * D * self._elt)
+        st = self._lib.rkv_append_decode(
+            lay, self._sal_struct, k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1),
+            pt.data_ptr(), self._free.data_ptr(), self._free_top, self._sal_init, qs,
+            decay, 1.0 - decay, float(scaling) if scaling else 0.0, os_, ws.data_ptr(), ws.numel(),
+            stream)
+        if obs is not None:
+            obs.after()
+        check(st, "rkv_append_decode")
+        if new_page:
+            self._free_top -= 1
+        self._n[layer_idx] = cur
+        self._seen_tokens = seen
+        self._layers[layer_idx].cumulative_length = seen
+        return out
+
     def _kv_bytes(self, layer_idx: int) -> int:
         """Bytes of retained K and V one attention pass over the layer reads."""
-        elt = torch.tensor([], dtype=self._dtype).element_size()
-        return 2 * self._B * self._Hkv * self._n[layer_idx] * self._D * elt
+        return 2 * self._B * self._Hkv * self._n[layer_idx] * self._D * self._elt
 
     def attention(self, query_states: torch.Tensor, layer_idx: int,
                   scaling: Optional[float] = None, is_causal: bool = False) -> torch.Tensor:
@@ -609,6 +705,7 @@ class PagedRazorKVCache(BaseCacheClass):
         self._pt.clear()
         self._layers.clear()
         self._seen_tokens = 0
+        self._lay_cache.clear()
         if self._k is not None:
             self._free = torch.arange(self._slots - 1, -1, -1, dtype=torch.int64, device=self._device)
             self._free_top = self._slots
@@ -619,6 +716,7 @@ class PagedRazorKVCache(BaseCacheClass):
         self._v = self._v.index_select(1, idx).contiguous()
         self._s = self._s.index_select(1, idx).contiguous()
         self._B = self._k.shape[1]
+        self._pool_changed()
 
     def batch_repeat_interleave(self, repeats: int) -> None:
         """razorkv/cache.py:198-206 (page tables are shared by every sequence)."""

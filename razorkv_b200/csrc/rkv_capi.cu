@@ -190,6 +190,16 @@ int rkv_append(const rkv_kv_layout* kv, const rkv_salience* sal, const void* k_n
     p.n_new = n_new; p.pos = pos;
     p.page_table = page_table; p.free_stack = free_stack; p.free_top = free_top;
     p.salience_init = salience_init;
+    {
+        const int64_t eb = kv->dtype == RKV_F32 ? 4 : 2;
+        const int64_t strides[7] = {new_stride_b, new_stride_h, new_stride_t, kv->stride_b,
+                                    kv->stride_h, kv->stride_p, kv->stride_t};
+        bool ok = (kv->head_dim * eb) % 16 == 0;
+        for (int64_t s : strides) ok = ok && (s * eb) % 16 == 0;
+        for (const void* ptr : {k_new, v_new, kv->k, kv->v})
+            ok = ok && (reinterpret_cast<uintptr_t>(ptr) & 15) == 0;
+        p.vec_ok = ok ? 1 : 0;
+    }
     return status_of(launch_append(p, S(stream)));
 }
 
@@ -242,6 +252,22 @@ int rkv_decode_fused(const rkv_query* q, const rkv_kv_layout* kv, const rkv_sali
     // shapes outside the fused kernel: the two shape-general kernels back to back
     if ((st = rkv_score(q, kv, sal, decay, one_minus_decay, 1, stream))) return st;
     return rkv_decode_attention(q, kv, scale, 0, out, workspace, workspace_bytes, stream);
+}
+
+int rkv_append_decode(const rkv_kv_layout* kv, const rkv_salience* sal, const void* k_new,
+                      const void* v_new, int64_t new_stride_b, int64_t new_stride_h,
+                      int64_t* page_table, const int64_t* free_stack, int64_t free_top,
+                      int salience_init, const rkv_query* q, float decay, float one_minus_decay,
+                      float scale, const rkv_output* out, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+    if (!kv) return RKV_ERR_INVALID_ARGUMENT;
+    int st = rkv_append(kv, sal, k_new, v_new, new_stride_b, new_stride_h, 0, 1, kv->num_tokens,
+                        page_table, free_stack, free_top, salience_init, stream);
+    if (st) return st;
+    rkv_kv_layout grown = *kv;
+    grown.num_tokens = kv->num_tokens + 1;
+    return rkv_decode_fused(q, &grown, sal, decay, one_minus_decay, scale, out, workspace,
+                            workspace_bytes, stream);
 }
 
 int rkv_page_scores(const rkv_kv_layout* kv, const rkv_salience* sal, int64_t first_token,

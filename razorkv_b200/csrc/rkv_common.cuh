@@ -5,9 +5,11 @@
 // computed in fp32.  Page selection is decided by these values, so every kernel that
 // produces them uses one fixed evaluation order that a CPU restatement can repeat exactly:
 // eight lanes cooperate on a row; lane j owns the 16-byte chunks c = j, j+8, j+16, ... of
-// the K row (CH = 16 / sizeof(K element) elements per chunk) and accumulates them in
-// ascending order with fused multiply-add starting from +0.0f; the eight partials are then
-// combined by an xor-4, xor-2, xor-1 butterfly, i.e.
+// the K row (CH = 16 / sizeof(K element) elements per chunk).  Listing the lane's elements
+// in ascending order, those at even positions accumulate into one chain and those at odd
+// positions into a second, each by fused multiply-add from +0.0f (the two halves of one
+// packed f32x2 FMA in the sm_100a kernel); the lane partial is even + odd.  The eight
+// partials are then combined by an xor-4, xor-2, xor-1 butterfly, i.e.
 //     ((p0 + p4) + (p2 + p6)) + ((p1 + p5) + (p3 + p7)).
 // fp32 addition is commutative, so every lane of the group ends with the same value.
 #pragma once

@@ -24,9 +24,10 @@
 //   3. (attend) runs the online softmax in the log2 domain with warp shuffles, stores the
 //      probabilities as bf16/fp16 and accumulates P.V with mma.sync m16n8k16 (Vt as the A
 //      operand straight from the swizzled stage via ldmatrix.trans, P^T as B).
-// At the end of a segment every warp writes its (m, l, acc) partial; the last CTA to finish
-// a sequence (atomic ticket, no waiting) merges the partials by log-sum-exp and writes the
-// output.  Tokens past N in the last page are masked and their V rows zeroed.
+// At the end of a segment every warp writes its (m, l, acc) partial; merge_kernel, launched
+// right after on the same stream, combines the partials of each (sequence, head) by
+// log-sum-exp with one CTA per row, so no SM sits in a serial merge tail.  Tokens past N in
+// the last page are masked and their V rows zeroed.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -44,10 +45,17 @@ namespace sm100 {
 
 constexpr int kComputeWarps = 8;
 constexpr int kComputeThreads = kComputeWarps * 32;
-constexpr int kThreads = kComputeThreads + 32;
+// Three warpgroups: two of compute warps and one whose first warp is the producer.  The
+// launch gives every thread 168 registers (384 x 168 = 64512); setmaxnreg then moves them to
+// the compute warpgroups: 256 x 224 + 128 x 56 = 64512, and per SM sub-partition (one warp
+// of each warpgroup) 2 x 32 x 224 + 32 x 56 = 16128 <= 16384.
+constexpr int kThreads = kComputeThreads + 128;
+constexpr int kComputeRegs = 224;
+constexpr int kProducerRegs = 56;
 constexpr int kTileTokens = 16;
 constexpr int kMaxStages = 6;
 constexpr int kSmemBudget = 200 * 1024;   // stage ring; the rest holds barriers and scratch
+constexpr float kRescaleLog2 = 8.0f;      // lazy softmax rescale threshold (log2 units)
 
 struct DevArgs {
     const void* q; int64_t q_stride_b, q_stride_h;
@@ -56,7 +64,7 @@ struct DevArgs {
     const int64_t* pt; int64_t pt_stride_b; int64_t num_slots;
     float* sal; int64_t sal_stride_b, sal_stride_p;
     float scale_r, logit_log2, decay, omd;
-    int attend, score;
+    int attend, score, sal_bulk;
     void* out; int64_t o_stride_b, o_stride_h;
     float* partials; int* counters; int* err;
     int stages, stage_bytes, tile_bytes, kv_tile_bytes, half_bytes;
@@ -71,6 +79,7 @@ struct SmemTail {             // placed after the stage ring
     int32_t redcnt[kMaxStages][kComputeWarps];
     uint16_t ps[kComputeWarps][8][kTileTokens];   // P (bf16/fp16) per warp: [head][token]
     float alpha[kComputeWarps][8];
+    alignas(16) float sal_old[kMaxStages][kComputeWarps][kTileTokens];   // bulk-copied salience rows
     int last;
     int abort;
 };
@@ -109,6 +118,26 @@ __device__ __forceinline__ void unpack8<__half>(uint4 w, float* f) {
         float2 t = __half22float2(*reinterpret_cast<const __half2*>(&u[i]));
         f[2 * i] = t.x;
         f[2 * i + 1] = t.y;
+    }
+}
+
+// The same 8 elements as 4 packed (even, odd) fp32 pairs for fma.rn.f32x2.
+template <typename T>
+__device__ __forceinline__ void unpack8_pairs(uint4 w, uint64_t* p);
+template <>
+__device__ __forceinline__ void unpack8_pairs<__nv_bfloat16>(uint4 w, uint64_t* p) {
+    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        p[i] = pack2(__uint_as_float(u[i] << 16), __uint_as_float(u[i] & 0xffff0000u));
+}
+template <>
+__device__ __forceinline__ void unpack8_pairs<__half>(uint4 w, uint64_t* p) {
+    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&u[i]));
+        p[i] = pack2(t.x, t.y);
     }
 }
 
@@ -189,49 +218,74 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
     const int Hkv = a.Hkv;
 
     // ------------------------------------------------------------------- producer warp
-    if (warp == kComputeWarps) {
-        if (lane != 0) return;
-        prefetch_tensormap(&tmk);
-        if (a.attend) prefetch_tensormap(&tmv);
-        uint32_t it = 0;
+    // The whole warp walks the schedule; lanes fetch the page ids of the next 32 tiles
+    // together and lane 0 issues the copies of each stage: the K (and V) boxes of every
+    // tile and, when scoring, the tile's 16 salience values (one 64-byte bulk copy) so the
+    // EWMA update never waits on a global load.
+    if (warp >= kComputeWarps) {
+        set_max_regs_dec<kProducerRegs>();
+        if (warp != kComputeWarps) return;   // the rest of the producer warpgroup idles out
+        if (lane == 0) {
+            prefetch_tensormap(&tmk);
+            if (a.attend) prefetch_tensormap(&tmv);
+        }
+        int slot = 0;
+        uint32_t par = 0;
         for (int64_t pos = r0; pos < r1;) {
             const int64_t b = pos / a.n_tiles;
             const int64_t seg_end = min(r1, (b + 1) * a.n_tiles);
             const int64_t tb0 = pos - b * a.n_tiles, tb1 = seg_end - b * a.n_tiles;
             const int64_t* ptb = a.pt + b * a.pt_stride_b;
-            for (int64_t t0 = tb0; t0 < tb1; t0 += wph, ++it) {
-                const int slot = it % NS;
-                const uint32_t par = (it / NS) & 1u;
-                if (!mbar_wait(&sm.empty[slot], par ^ 1u, a.err, &sm.abort)) return;
+            int64_t win = tb0;   // first tile of the page-id window held in registers
+            int64_t pid = (win + lane < tb1) ? __ldg(ptb + win + lane) : 0;
+            for (int64_t t0 = tb0; t0 < tb1; t0 += wph) {
                 const int ntile = (int)(tb1 - t0 < wph ? tb1 - t0 : wph);
-                uint8_t* st = smem + slot * a.stage_bytes;
-                for (int s = 0; s < ntile; ++s) {
-                    int64_t phys = __ldg(ptb + t0 + s);
-                    if (phys < 0 || phys >= a.num_slots) {
-                        if (a.err) atomicExch(a.err, 2);
-                        sm.phys[slot][s] = -1;
-                        phys = 0;
-                    } else {
-                        sm.phys[slot][s] = (int32_t)phys;
+                int32_t ph[kComputeWarps];
+#pragma unroll
+                for (int s = 0; s < kComputeWarps; ++s) {
+                    if (s < ntile) {
+                        const int64_t t = t0 + s;
+                        if (t >= win + 32) {   // slide the window (uniform across lanes)
+                            win = t;
+                            pid = (win + lane < tb1) ? __ldg(ptb + win + lane) : 0;
+                        }
+                        const int64_t v = __shfl_sync(0xffffffffu, pid, (int)(t - win));
+                        ph[s] = (v < 0 || v >= a.num_slots) ? -1 : (int32_t)v;
                     }
                 }
-                mbar_arrive_expect_tx(&sm.full[slot], (uint32_t)(ntile * a.tile_bytes));
-                for (int s = 0; s < ntile; ++s) {
-                    const int phys = max(sm.phys[slot][s], 0);
-                    int cc[3];
+                const bool ok = mbar_wait(&sm.empty[slot], par ^ 1u, a.err, &sm.abort);
+                if (lane == 0 && ok) {
+                    uint8_t* st = smem + slot * a.stage_bytes;
+                    uint32_t bytes = (uint32_t)(ntile * a.tile_bytes);
+                    for (int s = 0; s < ntile; ++s) {
+                        if (ph[s] < 0 && a.err) atomicExch(a.err, 2);
+                        sm.phys[slot][s] = ph[s];
+                    }
+                    if (a.score && a.sal_bulk) bytes += (uint32_t)(ntile * kTileTokens * 4);
+                    mbar_arrive_expect_tx(&sm.full[slot], bytes);
+                    for (int s = 0; s < ntile; ++s) {
+                        const int phys = max(ph[s], 0);
+                        int cc[3];
 #pragma unroll
-                    for (int k = 0; k < 3; ++k)
-                        cc[k] = a.role[k] == 0 ? 0 : a.role[k] == 1 ? (int)b : phys;
-                    uint8_t* tile = st + s * a.tile_bytes;
+                        for (int k = 0; k < 3; ++k)
+                            cc[k] = a.role[k] == 0 ? 0 : a.role[k] == 1 ? (int)b : phys;
+                        uint8_t* tile = st + s * a.tile_bytes;
 #pragma unroll
-                    for (int hf = 0; hf < HALVES; ++hf) {
-                        tma_load_5d(tile + hf * a.half_bytes, &tmk, &sm.full[slot], hf * 64, 0,
-                                    cc[0], cc[1], cc[2]);
-                        if (a.attend)
-                            tma_load_5d(tile + a.kv_tile_bytes + hf * a.half_bytes, &tmv,
-                                        &sm.full[slot], hf * 64, 0, cc[0], cc[1], cc[2]);
+                        for (int hf = 0; hf < HALVES; ++hf) {
+                            tma_load_5d(tile + hf * a.half_bytes, &tmk, &sm.full[slot], hf * 64, 0,
+                                        cc[0], cc[1], cc[2]);
+                            if (a.attend)
+                                tma_load_5d(tile + a.kv_tile_bytes + hf * a.half_bytes, &tmv,
+                                            &sm.full[slot], hf * 64, 0, cc[0], cc[1], cc[2]);
+                        }
+                        if (a.score && a.sal_bulk)
+                            bulk_load(&sm.sal_old[slot][s][0],
+                                      a.sal + (int64_t)phys * a.sal_stride_p + b * a.sal_stride_b,
+                                      kTileTokens * 4, &sm.full[slot]);
                     }
                 }
+                __syncwarp();
+                if (++slot == NS) { slot = 0; par ^= 1u; }
             }
             pos = seg_end;
         }
@@ -239,6 +293,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
     }
 
     // ------------------------------------------------------------------- compute warps
+    set_max_regs_inc<kComputeRegs>();
     const int h = warp % Hkv;       // kv head
     const int s = warp / Hkv;       // tile slot inside a stage
     const int g = lane >> 3, j = lane & 7;
@@ -247,9 +302,10 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
     const bool head_writer = (j & ((8 / GP) - 1)) == 0;   // one lane per head in each group
     const uint32_t ps_base = smem_u32(&sm.ps[warp][0][0]);
 
-    float qreg[GP][EPL];
+    uint64_t qreg[GP][EPL / 2];   // fl(q * scale) as (even, odd) element pairs
     float acc[MT][4];
-    uint32_t it = 0;
+    int slot = 0;
+    uint32_t par = 0;
     for (int64_t pos = r0; pos < r1;) {
         const int64_t b = pos / a.n_tiles;
         const int64_t seg_end = min(r1, (b + 1) * a.n_tiles);
@@ -260,11 +316,12 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
 #pragma unroll
         for (int i = 0; i < GP; ++i) {
 #pragma unroll
-            for (int e = 0; e < EPL; ++e) {
+            for (int e = 0; e < EPL; e += 2) {
                 const int dim = (e / 8) * 64 + 8 * j + (e % 8);
-                qreg[i][e] = i < G ? __fmul_rn(to_f<T>(qb[(int64_t)(h * G + i) * a.q_stride_h + dim]),
-                                               a.scale_r)
-                                   : 0.0f;
+                const T* qr = qb + (int64_t)(h * G + i) * a.q_stride_h + dim;
+                const float lo = i < G ? __fmul_rn(to_f<T>(qr[0]), a.scale_r) : 0.0f;
+                const float hi = i < G ? __fmul_rn(to_f<T>(qr[1]), a.scale_r) : 0.0f;
+                qreg[i][e / 2] = pack2(lo, hi);
             }
         }
         float m_run = -INFINITY, l_run = 0.0f;
@@ -273,11 +330,9 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
 #pragma unroll
             for (int e = 0; e < 4; ++e) acc[mt][e] = 0.0f;
 
-        for (int64_t t0 = tb0; t0 < tb1; t0 += wph, ++it) {
-            const int slot = it % NS;
-            const uint32_t par = (it / NS) & 1u;
+        for (int t0 = (int)tb0; t0 < (int)tb1; t0 += wph) {
             const bool landed = mbar_wait(&sm.full[slot], par, a.err, &sm.abort);
-            const int64_t tile = t0 + s;
+            const int tile = t0 + s;
             if (landed && tile < tb1) {
                 const int nv = (int)(a.N - tile * kTileTokens < kTileTokens ? a.N - tile * kTileTokens : kTileTokens);
                 uint8_t* tbase = smem + slot * a.stage_bytes + s * a.tile_bytes;
@@ -289,33 +344,50 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
 #pragma unroll
                 for (int r = 0; r < 4; ++r) {
                     const int t = 4 * r + g;
-                    float kf[EPL];
+                    uint64_t kp[EPL / 2];   // element pairs (even position, odd position)
 #pragma unroll
                     for (int hf = 0; hf < HALVES; ++hf) {
                         const uint4 w = lds128(kb + hf * a.half_bytes + t * 128 + ((j ^ (t & 7)) << 4));
-                        unpack8<T>(w, kf + hf * 8);
+                        unpack8_pairs<T>(w, kp + hf * 4);
                     }
                     float part[GP];
 #pragma unroll
                     for (int i = 0; i < GP; ++i) {
-                        float x = 0.0f;
+                        uint64_t x = 0ull;   // (+0.0f, +0.0f)
 #pragma unroll
-                        for (int e = 0; e < EPL; ++e) x = __fmaf_rn(qreg[i][e], kf[e], x);
-                        part[i] = x;
+                        for (int e = 0; e < EPL / 2; ++e) ffma2(x, qreg[i][e], kp[e]);
+                        part[i] = sum_pair(x);
                     }
                     sc[r] = group_transpose_reduce<GP>(part, j);
                 }
 
                 // ---- 2. resonance: max over this warp's heads, folded across kv heads ----
                 if (a.score) {
+                    // transpose-max over the 8 lanes of the group: afterwards lane j holds
+                    // the max over heads of round rj = 2*bit2(j) + bit1(j), i.e. token 4*rj + g
+                    uint32_t key[4];
 #pragma unroll
-                    for (int r = 0; r < 4; ++r) {
-                        const int t = 4 * r + g;
-                        uint32_t key = (t < nv && hl < G) ? ordered_key(sc[r]) : 0u;
-                        key = max(key, __shfl_xor_sync(0xffffffffu, key, 1));
-                        key = max(key, __shfl_xor_sync(0xffffffffu, key, 2));
-                        key = max(key, __shfl_xor_sync(0xffffffffu, key, 4));
-                        if (j == 0 && t < nv) atomicMax(&sm.red[slot][s][t], key);
+                    for (int r = 0; r < 4; ++r)
+                        key[r] = (4 * r + g < nv && hl < G) ? ordered_key(sc[r]) : 0u;
+                    {
+                        const bool up = (j & 4) != 0;
+#pragma unroll
+                        for (int i = 0; i < 2; ++i) {
+                            const uint32_t send = up ? key[i] : key[i + 2];
+                            const uint32_t keep = up ? key[i + 2] : key[i];
+                            key[i] = max(keep, __shfl_xor_sync(0xffffffffu, send, 4));
+                        }
+                    }
+                    {
+                        const bool up = (j & 2) != 0;
+                        const uint32_t send = up ? key[0] : key[1];
+                        const uint32_t keep = up ? key[1] : key[0];
+                        key[0] = max(keep, __shfl_xor_sync(0xffffffffu, send, 2));
+                    }
+                    key[0] = max(key[0], __shfl_xor_sync(0xffffffffu, key[0], 1));
+                    {
+                        const int t = 4 * (((j >> 2) & 1) * 2 + ((j >> 1) & 1)) + g;
+                        if ((j & 1) == 0 && t < nv) atomicMax(&sm.red[slot][s][t], key[0]);
                     }
                     __threadfence_block();
                     __syncwarp();
@@ -330,7 +402,8 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                             if (lane < nv && phys >= 0) {
                                 float* sp = a.sal + (int64_t)phys * a.sal_stride_p + b * a.sal_stride_b + lane;
                                 const float R = key_to_float(key);
-                                *sp = __fadd_rn(__fmul_rn(a.decay, *sp), __fmul_rn(a.omd, R));
+                                const float old = a.sal_bulk ? sm.sal_old[slot][s][lane] : *sp;
+                                *sp = __fadd_rn(__fmul_rn(a.decay, old), __fmul_rn(a.omd, R));
                             }
                             sm.red[slot][s][lane] = 0u;
                         }
@@ -350,19 +423,27 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                     }
                     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
                     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-                    const float m_new = fmaxf(m_run, mx);
-                    const bool live = m_new != -INFINITY;
-                    const float alpha = live ? ex2(m_run - m_new) : 1.0f;
+                    // Lazy rescaling: the running reference max only moves when the tile max
+                    // exceeds it by more than 2^8, so P stays <= 256 (exact range for bf16/fp16
+                    // and fp32 sums) and the accumulator is rescaled only on those rare tiles.
+                    const bool raise = mx > m_run + kRescaleLog2;   // includes m_run == -inf
+                    const bool any_raise = __any_sync(0xffffffffu, raise);
+                    if (any_raise) {
+                        const float m_new = raise ? mx : m_run;
+                        const float alpha = raise ? ex2(m_run - m_new) : 1.0f;   // ex2(-inf) = 0
+                        l_run *= alpha;
+                        m_run = m_new;
+                        if (head_writer && g == 0) sm.alpha[warp][hl] = alpha;
+                    }
+                    const bool live = m_run != -INFINITY;
                     float psum = 0.0f;
 #pragma unroll
                     for (int r = 0; r < 4; ++r) {
-                        const float p = live ? ex2(z[r] - m_new) : 0.0f;
+                        const float p = live ? ex2(z[r] - m_run) : 0.0f;
                         psum += p;
                         if (head_writer) sm.ps[warp][hl][4 * r + g] = to_bits<T>(p);
                     }
-                    l_run = l_run * alpha + psum;
-                    m_run = m_new;
-                    if (head_writer && g == 0) sm.alpha[warp][hl] = alpha;
+                    l_run += psum;
                     if (nv < kTileTokens) {
                         // zero V rows past the last valid token (their P is 0; keep them finite)
                         for (int i = lane; i < (kTileTokens - nv) * 8 * HALVES; i += 32) {
@@ -375,11 +456,13 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                     }
                     __syncwarp();
                     const int n0 = 2 * (lane & 3);
-                    const float al0 = sm.alpha[warp][n0], al1 = sm.alpha[warp][n0 + 1];
+                    if (any_raise) {
+                        const float al0 = sm.alpha[warp][n0], al1 = sm.alpha[warp][n0 + 1];
 #pragma unroll
-                    for (int mt = 0; mt < MT; ++mt) {
-                        acc[mt][0] *= al0; acc[mt][1] *= al1;
-                        acc[mt][2] *= al0; acc[mt][3] *= al1;
+                        for (int mt = 0; mt < MT; ++mt) {
+                            acc[mt][0] *= al0; acc[mt][1] *= al1;
+                            acc[mt][2] *= al0; acc[mt][3] *= al1;
+                        }
                     }
                     const uint32_t b0 = lds32(ps_base + ((lane >> 2) * kTileTokens + n0) * 2);
                     const uint32_t b1 = lds32(ps_base + ((lane >> 2) * kTileTokens + n0 + 8) * 2);
@@ -398,20 +481,23 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&sm.empty[slot]);
+            if (++slot == NS) { slot = 0; par ^= 1u; }
         }
 
-        // ---- segment end: write partial, last CTA of the sequence merges -----------------
+        // ---- segment end: write this warp's partial --------------------------------------
+        // partial row per query head: acc[0, D) | m (log2 units) at D | l at D+1 | pad;
+        // merge_kernel combines the partials of a sequence once the whole grid is done
         if (a.attend) {
+            constexpr int RS = D + 4;
             float l_tot = l_run + __shfl_xor_sync(0xffffffffu, l_run, 8);
             l_tot += __shfl_xor_sync(0xffffffffu, l_tot, 16);
             const int64_t cfirst = (b * a.n_tiles) / a.W;
-            const int64_t clast = ((b + 1) * a.n_tiles - 1) / a.W;
             const int64_t pidx = (c - cfirst) * wph + s;
-            float* part = a.partials + ((b * a.maxc * wph + pidx) * a.Hq) * (int64_t)(D + 2);
+            float* part = a.partials + ((b * a.maxc * wph + pidx) * a.Hq) * (int64_t)RS;
             if (head_writer && g == 0 && hl < G) {
-                float* ph = part + (int64_t)(h * G + hl) * (D + 2);
-                ph[0] = m_run;
-                ph[1] = l_tot;
+                float* ph = part + (int64_t)(h * G + hl) * RS;
+                ph[D] = m_run;
+                ph[D + 1] = l_tot;
             }
             const int n0 = 2 * (lane & 3);
 #pragma unroll
@@ -421,45 +507,63 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                 for (int e = 0; e < 4; ++e) {
                     const int n = n0 + (e & 1);
                     const int d = d0 + (e >> 1) * 8;
-                    if (n < G) part[(int64_t)(h * G + n) * (D + 2) + 2 + d] = acc[mt][e];
+                    if (n < G) part[(int64_t)(h * G + n) * RS + d] = acc[mt][e];
                 }
             }
-            __threadfence();
-            compute_barrier(kComputeThreads);
-            if (threadIdx.x == 0) {
-                const int nparts = (int)(clast - cfirst + 1);
-                const int old = atomicAdd(&a.counters[b], 1);
-                sm.last = old == nparts - 1;
-                if (sm.last) a.counters[b] = 0;
-            }
-            compute_barrier(kComputeThreads);
-            const bool last = sm.last;
-            if (last) {
-                __threadfence();
-                const int np = (int)(clast - cfirst + 1) * wph;
-                const float* pb = a.partials + (b * a.maxc * wph) * a.Hq * (int64_t)(D + 2);
-                T* ob = static_cast<T*>(a.out) + b * a.o_stride_b;
-                for (int idx = threadIdx.x; idx < a.Hq * D; idx += kComputeThreads) {
-                    const int hq = idx / D, d = idx % D;
-                    float M = -INFINITY;
-                    for (int p = 0; p < np; ++p)
-                        M = fmaxf(M, __ldcg(pb + ((int64_t)p * a.Hq + hq) * (D + 2)));
-                    float L = 0.f, O = 0.f;
-                    for (int p = 0; p < np; ++p) {
-                        const float* ph = pb + ((int64_t)p * a.Hq + hq) * (D + 2);
-                        const float mp = __ldcg(ph);
-                        if (mp == -INFINITY) continue;
-                        const float w = ex2(mp - M);
-                        L += __ldcg(ph + 1) * w;
-                        O += __ldcg(ph + 2 + d) * w;
-                    }
-                    ob[(int64_t)hq * a.o_stride_h + d] = from_f<T>(L > 0.f ? O / L : 0.f);
-                }
-            }
-            compute_barrier(kComputeThreads);
         }
         pos = seg_end;
     }
+}
+
+// Log-sum-exp merge of the per-warp partials: one CTA per (sequence, query head), one lane
+// per output dimension; every partial's (m, l, acc[d]) is loaded at once (no dependent
+// round-trips), weights 2^(m_p - M) go through shuffles.
+struct MergeArgs {
+    const float* partials; void* out; int64_t o_stride_b, o_stride_h;
+    int Hq, wph; int64_t n_tiles, W, maxc;
+};
+
+template <typename T, int D>
+__global__ void __launch_bounds__(D)
+merge_kernel(const MergeArgs a) {
+    constexpr int RS = D + 4;
+    const int lane = threadIdx.x & 31;
+    const int d = threadIdx.x;
+    const int64_t b = blockIdx.x / a.Hq;
+    const int hq = blockIdx.x % a.Hq;
+    const int64_t cfirst = (b * a.n_tiles) / a.W;
+    const int64_t clast = ((b + 1) * a.n_tiles - 1) / a.W;
+    const int np = (int)(clast - cfirst + 1) * a.wph;
+    const float* pb = a.partials + ((b * a.maxc * a.wph) * a.Hq + hq) * (int64_t)RS;
+    const int64_t pstride = (int64_t)a.Hq * RS;
+    float M = -INFINITY, O = 0.f, L = 0.f;
+    for (int p0 = 0; p0 < np; p0 += 32) {
+        const int n = min(32, np - p0);
+        // lane p holds the stats of partial p0 + p
+        const float mp = lane < n ? __ldcg(pb + (p0 + lane) * pstride + D) : -INFINITY;
+        const float lp = lane < n ? __ldcg(pb + (p0 + lane) * pstride + D + 1) : 0.f;
+        float acc[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[i] = i < n ? __ldcg(pb + (p0 + i) * pstride + d) : 0.f;
+        float Mc = mp;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) Mc = fmaxf(Mc, __shfl_xor_sync(0xffffffffu, Mc, o));
+        const float Mn = fmaxf(M, Mc);
+        if (Mn == -INFINITY) continue;
+        const float r = M == -INFINITY ? 0.f : ex2(M - Mn);
+        const float wl = mp == -INFINITY ? 0.f : ex2(mp - Mn);
+        float Lc = lp * wl;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) Lc += __shfl_xor_sync(0xffffffffu, Lc, o);
+        float Oc = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) Oc += acc[i] * __shfl_sync(0xffffffffu, wl, i);
+        O = O * r + Oc;
+        L = L * r + Lc;
+        M = Mn;
+    }
+    T* ob = static_cast<T*>(a.out) + b * a.o_stride_b + (int64_t)hq * a.o_stride_h;
+    ob[d] = from_f<T>(L > 0.f ? O / L : 0.f);
 }
 
 // ------------------------------------------------------------------------------ host side
@@ -561,13 +665,20 @@ static cudaError_t launch_t(const FusedParams& f, const Plan& pl, CUtensorMapDat
     a.scale_r = f.scale_r; a.logit_log2 = f.logit_mul * 1.4426950408889634f;
     a.decay = f.decay; a.omd = f.one_minus_decay;
     a.attend = f.attend; a.score = f.sal != nullptr;
+    a.sal_bulk = f.sal && !(reinterpret_cast<uintptr_t>(f.sal) & 15) && !((f.sal_stride_b * 4) & 15) &&
+                 !((f.sal_stride_p * 4) & 15);
     a.out = f.out; a.o_stride_b = f.o_stride_b; a.o_stride_h = f.o_stride_h;
     a.partials = f.partials; a.counters = f.counters; a.err = f.err;
     a.stages = pl.stages; a.stage_bytes = pl.stage_bytes; a.tile_bytes = pl.tile_bytes;
     a.kv_tile_bytes = pl.kv_tile_bytes; a.half_bytes = pl.half_bytes;
     for (int i = 0; i < 3; ++i) a.role[i] = role[i];
     kern<<<(unsigned)pl.grid, kThreads, pl.smem_bytes, stream>>>(mk, mv, a);
-    return cudaGetLastError();
+    cudaError_t e = counted(cudaGetLastError(), 1);
+    if (e != cudaSuccess || !f.attend) return e;
+    MergeArgs m{f.partials, f.out, f.o_stride_b, f.o_stride_h, f.Hq, pl.wph, pl.n_tiles, pl.W,
+                pl.maxc};
+    merge_kernel<T, D><<<(unsigned)(f.B * f.Hq), D, 0, stream>>>(m);
+    return counted(cudaGetLastError(), 1);
 }
 
 }  // namespace sm100
@@ -591,7 +702,7 @@ bool fused_supported(int dtype, int D, int Hkv, int Hq, int64_t page_size, int64
 size_t fused_workspace_bytes(int64_t B, int Hq, int Hkv, int D, int64_t N) {
     if (B <= 0 || Hkv <= 0) return 0;
     sm100::Plan pl = sm100::make_plan(B, N, Hkv, D, true);
-    return (size_t)B * pl.maxc * pl.wph * Hq * (D + 2) * sizeof(float);
+    return (size_t)B * pl.maxc * pl.wph * Hq * (D + 4) * sizeof(float);
 }
 
 cudaError_t launch_fused(const FusedParams& p, cudaStream_t st) {
@@ -615,7 +726,7 @@ cudaError_t launch_fused(const FusedParams& p, cudaStream_t st) {
         else e = G <= 4 ? launch_t<__half, 64, 4>(p, pl, dt, st)
                         : launch_t<__half, 64, 8>(p, pl, dt, st);
     }
-    return counted(e, 1);
+    return e;
 }
 
 }  // namespace rkv

@@ -79,10 +79,13 @@ score_kernel(ScoreParams p) {
                     for (int e = 0; e < ne; ++e) kr[e] = 0.0f;
                 }
                 for (int r = 0; r < nr; ++r) {
-                    float acc = 0.0f;
+                    float ev = 0.0f, od = 0.0f;   // even / odd positions of the lane's elements
                     const float* qr = qs + r * D;
-                    for (int e = 0; e < ne; ++e) acc = __fmaf_rn(qr[idx[e]], kr[e], acc);
-                    const float s = group8_sum(acc);
+                    for (int e = 0; e < ne; ++e) {
+                        if (e & 1) od = __fmaf_rn(qr[idx[e]], kr[e], od);
+                        else ev = __fmaf_rn(qr[idx[e]], kr[e], ev);
+                    }
+                    const float s = group8_sum(__fadd_rn(ev, od));
                     if (valid) best[it] = max(best[it], ordered_key(s));
                 }
             }
@@ -379,48 +382,99 @@ compact_pages_kernel(int64_t* pt, int64_t sink_pages, int64_t num_pages, const i
 
 // ------------------------------------------------------------------------------------------
 // Append (razorkv/cache.py:239-247, 369-390): write rows, initial salience, new page ids.
-// One 8-lane group per (b, token); the group copies the K and V rows of every kv head and
-// reduces sum_h sqrt(canonical k.k) in ascending h.
+// Work item = (sequence b, new token i); 256 threads = 32 groups of 8 lanes.  With Hkv <= 32
+// a CTA takes 32 / Hkv items and group g serves kv head g % Hkv of item g / Hkv; with more
+// heads a CTA takes one item and its groups stride over the heads.  A group copies its K and
+// V rows (16-byte vectors when aligned), computes sqrt(canonical k.k) and leaves it in
+// shared memory; one thread per item then sums the heads in ascending order and divides.
 // ------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(256)
-append_kernel(AppendParams p) {
-    const int lane = threadIdx.x & 31, j = lane & 7;
-    const int64_t gidx = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 3;
-    const bool active = gidx < p.n_new * p.B;
-    const int64_t b = active ? gidx / p.n_new : 0;
-    const int64_t i = active ? gidx % p.n_new : 0;
-    const int64_t t = p.pos + i;
+constexpr int kAppendThreads = 256;
+constexpr int kAppendGroups = kAppendThreads / 8;
+
+__device__ __forceinline__ int64_t append_phys(const AppendParams& p, int64_t t) {
     const int64_t P = p.page_size;
     const int64_t first_new_page = (p.pos + P - 1) / P;
     const int64_t lp = t / P;
-    int64_t phys = 0;
-    if (active) {
-        phys = lp < first_new_page ? p.page_table[lp]
-                                   : p.free_stack[p.free_top - 1 - (lp - first_new_page)];
-        if (b == 0 && j == 0 && lp >= first_new_page && t % P == 0) p.page_table[lp] = phys;
+    return lp < first_new_page ? p.page_table[lp]
+                               : p.free_stack[p.free_top - 1 - (lp - first_new_page)];
+}
+
+__global__ void __launch_bounds__(kAppendThreads)
+append_kernel(AppendParams p) {
+    extern __shared__ float nrm[];   // [items per CTA][Hkv]
+    const int lane = threadIdx.x & 31, j = lane & 7, grp = threadIdx.x >> 3;
+    const int hk = p.Hkv;
+    const int ipc = hk >= kAppendGroups ? 1 : kAppendGroups / hk;   // items per CTA
+    const int li = hk >= kAppendGroups ? 0 : grp / hk;              // local item
+    const int h0 = hk >= kAppendGroups ? grp : grp % hk;
+    const int hstep = hk >= kAppendGroups ? kAppendGroups : hk;
+    const int64_t item = (int64_t)blockIdx.x * ipc + li;
+    const bool active = li < ipc && item < p.n_new * p.B;
+    const int64_t b = active ? item / p.n_new : 0;
+    const int64_t i = active ? item % p.n_new : 0;
+    const int64_t t = p.pos + i;
+    const int64_t P = p.page_size;
+    const int64_t phys = active ? append_phys(p, t) : 0;
+    if (active && h0 == 0 && j == 0 && b == 0 && t % P == 0) {
+        const int64_t lp = t / P;
+        if (lp >= (p.pos + P - 1) / P) p.page_table[lp] = phys;
     }
-    const int ch = 16 / elt_bytes(p.dtype);
-    int idx[kLaneElts];
-    const int ne = lane_elements(p.D, ch, j, idx);
-    float norm_sum = 0.0f;
-    for (int h = 0; h < p.Hkv; ++h) {
-        float part = 0.0f;
+    const int eb = elt_bytes(p.dtype);
+    const int ch = 16 / eb;
+    // 16-byte vector path: every row start 16-byte aligned and D a whole number of chunks
+    const bool vec = p.vec_ok;
+    for (int h = h0; h < hk; h += hstep) {
+        float ev = 0.0f, od = 0.0f;   // canonical even / odd sub-chains of k.k
         if (active) {
             const int64_t src = b * p.new_stride_b + (int64_t)h * p.new_stride_h + i * p.new_stride_t;
             const int64_t dst = b * p.stride_b + (int64_t)h * p.stride_h + phys * p.stride_p +
                                 (t % P) * p.stride_t;
-            for (int e = 0; e < ne; ++e) {
-                float kv = load_elt(p.k_new, src + idx[e], p.dtype);
-                store_elt(p.k, dst + idx[e], p.dtype, kv);
-                store_elt(p.v, dst + idx[e], p.dtype, load_elt(p.v_new, src + idx[e], p.dtype));
-                part = __fmaf_rn(kv, kv, part);
+            if (vec) {
+                int pos = 0;
+                for (int c = j; c * ch < p.D; c += 8) {
+                    const uint4 kw = *reinterpret_cast<const uint4*>(
+                        static_cast<const char*>(p.k_new) + (src + (int64_t)c * ch) * eb);
+                    const uint4 vw = *reinterpret_cast<const uint4*>(
+                        static_cast<const char*>(p.v_new) + (src + (int64_t)c * ch) * eb);
+                    *reinterpret_cast<uint4*>(static_cast<char*>(p.k) + (dst + (int64_t)c * ch) * eb) = kw;
+                    *reinterpret_cast<uint4*>(static_cast<char*>(p.v) + (dst + (int64_t)c * ch) * eb) = vw;
+                    const uint32_t u[4] = {kw.x, kw.y, kw.z, kw.w};
+                    for (int e = 0; e < ch; ++e, ++pos) {
+                        float kv;
+                        if (eb == 4) kv = __uint_as_float(u[e]);
+                        else if (p.dtype == RKV_BF16)
+                            kv = __uint_as_float((e & 1) ? (u[e >> 1] & 0xffff0000u) : (u[e >> 1] << 16));
+                        else {
+                            const __half2 hv = *reinterpret_cast<const __half2*>(&u[e >> 1]);
+                            kv = (e & 1) ? __high2float(hv) : __low2float(hv);
+                        }
+                        if (pos & 1) od = __fmaf_rn(kv, kv, od);
+                        else ev = __fmaf_rn(kv, kv, ev);
+                    }
+                }
+            } else {
+                int idx[kLaneElts];
+                const int ne = lane_elements(p.D, ch, j, idx);
+                for (int e = 0; e < ne; ++e) {
+                    const float kv = load_elt(p.k_new, src + idx[e], p.dtype);
+                    store_elt(p.k, dst + idx[e], p.dtype, kv);
+                    store_elt(p.v, dst + idx[e], p.dtype, load_elt(p.v_new, src + idx[e], p.dtype));
+                    if (e & 1) od = __fmaf_rn(kv, kv, od);
+                    else ev = __fmaf_rn(kv, kv, ev);
+                }
             }
         }
-        float ss = group8_sum(part);
-        norm_sum = __fadd_rn(norm_sum, __fsqrt_rn(ss));
+        const float ss = group8_sum(__fadd_rn(ev, od));
+        if (active && j == 0) nrm[li * hk + h] = __fsqrt_rn(ss);
     }
-    if (active && j == 0) {
-        float s0 = p.salience_init == RKV_SAL_NORM ? __fdiv_rn(norm_sum, (float)p.Hkv) : 1.0f;
+    __syncthreads();
+    if (active && h0 == 0 && j == 0) {
+        float s0 = 1.0f;
+        if (p.salience_init == RKV_SAL_NORM) {
+            float acc = 0.0f;
+            for (int h = 0; h < hk; ++h) acc = __fadd_rn(acc, nrm[li * hk + h]);
+            s0 = __fdiv_rn(acc, (float)hk);
+        }
         p.sal[phys * p.sal_stride_p + b * p.sal_stride_b + t % P] = s0;
     }
 }
@@ -577,9 +631,11 @@ cudaError_t launch_compact_pages(int64_t* pt, int64_t sink_pages, int64_t num_pa
 }
 
 cudaError_t launch_append(const AppendParams& p, cudaStream_t st) {
-    int64_t groups = p.n_new * p.B;
-    if (groups == 0) return cudaSuccess;
-    append_kernel<<<(unsigned)((groups * 8 + 255) / 256), 256, 0, st>>>(p);
+    const int64_t items = p.n_new * p.B;
+    if (items == 0) return cudaSuccess;
+    const int ipc = p.Hkv >= kAppendGroups ? 1 : kAppendGroups / p.Hkv;
+    const size_t smem = (size_t)ipc * p.Hkv * sizeof(float);
+    append_kernel<<<(unsigned)((items + ipc - 1) / ipc), kAppendThreads, smem, st>>>(p);
     return counted(cudaGetLastError(), 1);
 }
 

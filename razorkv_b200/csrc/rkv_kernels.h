@@ -51,6 +51,7 @@ struct AppendParams {
     int64_t n_new, pos;
     int64_t* page_table; const int64_t* free_stack; int64_t free_top;
     int salience_init;
+    int vec_ok;   // every row 16-byte aligned and D a whole number of 16-byte chunks
 };
 
 struct CompactTokensParams {

@@ -19,13 +19,16 @@ def test_canonical_dot_order_definition():
         # restate the order in numpy float32 with an exact fma (via float64 product + one rounding)
         p = []
         for j in range(8):
-            acc = np.float32(0.0)
+            chains = [np.float32(0.0), np.float32(0.0)]   # even / odd positions
+            pos = 0
             c = j
             while c * ch < D:
                 for e in range(c * ch, min(D, c * ch + ch)):
-                    acc = np.float32(np.float64(a[e]) * np.float64(b[e]) + np.float64(acc))
+                    acc = chains[pos & 1]
+                    chains[pos & 1] = np.float32(np.float64(a[e]) * np.float64(b[e]) + np.float64(acc))
+                    pos += 1
                 c += 8
-            p.append(acc)
+            p.append(np.float32(chains[0] + chains[1]))
         f = np.float32
         expect = f(f(f(p[0] + p[4]) + f(p[2] + p[6])) + f(f(p[1] + p[5]) + f(p[3] + p[7])))
         assert O.canon_dot(a, b, elt) == expect
