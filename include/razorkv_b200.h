@@ -130,6 +130,17 @@ int rkv_decode_attention(const rkv_query* q, const rkv_kv_layout* kv, float scal
                          const rkv_output* out, void* workspace, size_t workspace_bytes,
                          void* stream);
 
+/* rkv_decode_attention without a caller workspace.  No counterpart in the reference: it
+ * serves callers that cannot allocate device memory when they call (a host framework that
+ * owns the whole device heap, or a decode loop that must not enter the driver's allocator).
+ * Its scratch is a fixed RKV_NOALLOC_SCRATCH_BYTES array built into the library, held on
+ * every device that loads it; calls needing more return RKV_ERR_WORKSPACE_TOO_SMALL without
+ * launching.  The first call on a device looks up the array's device address, so make it
+ * before any stream capture.  All calls share the array: calls that overlap on the GPU race. */
+#define RKV_NOALLOC_SCRATCH_BYTES (16u << 20)
+int rkv_decode_attention_noalloc(const rkv_query* q, const rkv_kv_layout* kv, float scale,
+                                 int causal, const rkv_output* out, void* stream);
+
 /* ---- page pooling -----------------------------------------------------------------------
  * out[b, p] = max (or mean) of sal[b*stride_b + p*page_size + i], i < page_size, for
  * p < S / page_size (when S < page_size: out[b, 0] = max over the row). */

@@ -64,6 +64,8 @@ _SIGNATURES = {
     "rkv_decode_attention_workspace_size": (c_sz, [P(Query), P(KVLayout)]),
     "rkv_decode_attention": (ctypes.c_int, [P(Query), P(KVLayout), c_f32, ctypes.c_int,
                                             P(Output), c_vp, c_sz, c_vp]),
+    "rkv_decode_attention_noalloc": (ctypes.c_int, [P(Query), P(KVLayout), c_f32, ctypes.c_int,
+                                                    P(Output), c_vp]),
     "rkv_page_salience_pool": (ctypes.c_int, [c_vp, c_i64, c_i64, c_i64, c_i64, ctypes.c_int,
                                               c_vp, c_vp]),
     "rkv_append": (ctypes.c_int, [P(KVLayout), P(Salience), c_vp, c_vp, c_i64, c_i64, c_i64,

@@ -19,7 +19,7 @@ OBJ_DIR = os.path.join(HERE, "_build")
 LIB_DIR = os.path.join(HERE, "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "librazorkv_b200.so")
 
-SOURCES = ["rkv_capi.cu", "rkv_generic.cu", "rkv_decode_sm100.cu"]
+SOURCES = ["rkv_capi.cu", "rkv_generic.cu", "rkv_decode_sm100.cu", "rkv_noalloc.cu"]
 HEADERS = ["rkv_common.cuh", "rkv_kernels.h", "rkv_sm100.cuh"]
 
 NVCC_FLAGS = [

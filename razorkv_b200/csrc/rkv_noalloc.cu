@@ -1,0 +1,63 @@
+// Decode attention for callers that cannot allocate device memory.
+//
+// rkv_decode_attention needs a caller-provided workspace for its split-K partials.  Some
+// callers have no way to provide one at call time: code running inside a host framework
+// that owns the whole device heap and forbids allocations outside its arena, or a serving
+// loop that must not take the driver's allocation path (which can synchronise the device)
+// between two decode steps.  rkv_decode_attention_noalloc serves them from a fixed scratch
+// array compiled into this library instead.
+//
+// The array below is a file-scope device variable: every GPU that loads the library holds
+// RKV_NOALLOC_SCRATCH_BYTES of it until the process exits.  Host code cannot use the array's
+// name as a device address (on the host it names a host-side stand-in), so the first call on
+// each device looks up the real device address with cudaGetSymbolAddress while that device is
+// current and keeps it; make that first call before any stream capture.  The array is shared
+// by every call on the device and keeps the previous call's contents, so each call clears the
+// part that must start at zero (the workspace header: error flag and merge counters) on its
+// stream before launching.  Calls whose kernels overlap on the GPU (different streams, or
+// different host threads) race on the array; serialise them.
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "../../include/razorkv_b200.h"
+
+namespace {
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[RKV_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_mu;
+void* g_ptr[kMaxDevices] = {nullptr};
+
+// Device address of the scratch array on the current device (looked up once per device).
+int scratch_address(void** out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return RKV_ERR_CUDA;
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!g_ptr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return RKV_ERR_CUDA;
+        g_ptr[dev] = p;
+    }
+    *out = g_ptr[dev];
+    return RKV_OK;
+}
+
+}  // namespace
+
+extern "C" int rkv_decode_attention_noalloc(const rkv_query* q, const rkv_kv_layout* kv,
+                                            float scale, int causal, const rkv_output* out,
+                                            void* stream) {
+    if (!q || !kv || !out) return RKV_ERR_INVALID_ARGUMENT;
+    const size_t need = rkv_decode_attention_workspace_size(q, kv);
+    if (need > (size_t)RKV_NOALLOC_SCRATCH_BYTES) return RKV_ERR_WORKSPACE_TOO_SMALL;
+    void* ws = nullptr;
+    int st = scratch_address(&ws);
+    if (st) return st;
+    if (cudaMemsetAsync(ws, 0, RKV_WORKSPACE_HEADER_BYTES, static_cast<cudaStream_t>(stream)) !=
+        cudaSuccess)
+        return RKV_ERR_CUDA;
+    return rkv_decode_attention(q, kv, scale, causal, out, ws, (size_t)RKV_NOALLOC_SCRATCH_BYTES,
+                                stream);
+}
