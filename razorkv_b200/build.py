@@ -65,7 +65,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
                 sys.stdout.write(res.stderr)
     if force or _stale(LIB_PATH, objs):
         cmd = [_nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", LIB_PATH,
-               *objs, "-lcuda"]
+               *objs]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             sys.stderr.write(res.stdout + res.stderr)

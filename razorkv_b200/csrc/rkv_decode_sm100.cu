@@ -605,6 +605,26 @@ static Plan make_plan(int64_t B, int64_t N, int Hkv, int D, bool attend) {
     return p;
 }
 
+// The driver's tensor-map encoder, looked up through the runtime so the library does not
+// link libcuda (it loads on hosts without a driver; the lookup happens at the first launch).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_tiled_fn() {
+    static EncodeTiledFn fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return static_cast<EncodeTiledFn>(nullptr);
+        return reinterpret_cast<EncodeTiledFn>(p);
+    }();
+    return fn;
+}
+
 // 5-D map over one K or V storage: dims (D, 16 tokens, then kv head / sequence / page slot
 // in ascending stride order); the box covers 64 elements x 16 tokens x all kv heads, so it
 // lands in shared memory as [Hkv][16][64] whatever the storage order.  role[] reports which
@@ -625,11 +645,11 @@ static bool encode_map(CUtensorMap* map, const void* base, CUtensorMapDataType d
                                (cuuint32_t)outer[1].box, (cuuint32_t)outer[2].box};
     const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
     for (int i = 0; i < 3; ++i) role[i] = outer[i].role;
-    CUresult r = cuTensorMapEncodeTiled(map, dt, 5, const_cast<void*>(base), dims, strides, box,
-                                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                                        CU_TENSOR_MAP_SWIZZLE_128B,
-                                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    const EncodeTiledFn encode = encode_tiled_fn();
+    if (!encode) return false;
+    CUresult r = encode(map, dt, 5, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
 

@@ -1,0 +1,49 @@
+"""The C-ABI library loads and exports every function include/razorkv_b200.h declares (CPU;
+no kernel is launched)."""
+
+import os
+import re
+
+from razorkv_b200 import _lib
+
+ROOT = os.path.abspath(os.path.join(os.path.dirname(__file__), ".."))
+
+
+def _declared():
+    with open(os.path.join(ROOT, "include", "razorkv_b200.h")) as f:
+        src = f.read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(rkv_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    assert "rkv_decode_attention" in names and "rkv_append_decode" in names
+    assert len(names) >= 15
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in _declared():
+        assert hasattr(lib, name), f"{name} declared in the header but not exported"
+
+
+def test_binding_covers_every_declared_symbol():
+    assert sorted(_lib.EXPORTED) == _declared()
+
+
+def test_status_strings_and_version():
+    lib = _lib.load()
+    assert lib.rkv_abi_version() == 1
+    assert lib.rkv_status_string(0) == b"ok"
+    assert lib.rkv_status_string(4) == b"free page list exhausted"
+    assert lib.rkv_workspace_error_flag_offset() == 0
+
+
+def test_argument_errors_without_a_device():
+    """Validation happens before any CUDA call, so bad arguments are reported on a CPU host."""
+    lib = _lib.load()
+    assert lib.rkv_select_pages(None, 1, 4, 2, None, None, None, 0, None) == 1
+    assert lib.rkv_compact_pages(None, 0, 1, None, 1, 1, 1, None, 0, None) == 1
+    assert lib.rkv_release_pages(None, 3, None, 0, None) == 1
+    assert lib.rkv_page_salience_pool(None, 1, 8, 8, 4, 0, None, None) == 1
