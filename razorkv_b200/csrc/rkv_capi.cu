@@ -261,11 +261,31 @@ int rkv_append_decode(const rkv_kv_layout* kv, const rkv_salience* sal, const vo
                       float scale, const rkv_output* out, void* workspace, size_t workspace_bytes,
                       void* stream) {
     if (!kv) return RKV_ERR_INVALID_ARGUMENT;
-    int st = rkv_append(kv, sal, k_new, v_new, new_stride_b, new_stride_h, 0, 1, kv->num_tokens,
-                        page_table, free_stack, free_top, salience_init, stream);
-    if (st) return st;
     rkv_kv_layout grown = *kv;
     grown.num_tokens = kv->num_tokens + 1;
+    // One kernel does the append, the scoring and the attention when the fused kernel covers
+    // the shape and the new rows are 16-byte vectors; otherwise append, then score + attend.
+    int st = check_kv(&grown, true);
+    if (st) return st;
+    if ((st = check_q(q, &grown))) return st;
+    const bool rows_aligned = k_new && v_new && !(reinterpret_cast<uintptr_t>(k_new) & 15) &&
+                              !(reinterpret_cast<uintptr_t>(v_new) & 15) &&
+                              !((new_stride_b * 2) & 15) && !((new_stride_h * 2) & 15);
+    if (sal && sal->s && out && out->out && page_table && free_stack && grown.batch > 0 &&
+        grown.page_table == page_table && grown.pt_stride_b == 0 && rows_aligned &&
+        fast_ok(q, &grown, true) && (kv->num_tokens % kv->page_size != 0 || free_top >= 1)) {
+        if (workspace_bytes < rkv_decode_fused_workspace_size(q, &grown) || !workspace)
+            return RKV_ERR_WORKSPACE_TOO_SMALL;
+        FusedParams p = fused_params(q, &grown, sal, decay, one_minus_decay, scale, out);
+        p.partials = ws_body(workspace); p.counters = ws_counters(workspace); p.err = ws_err(workspace);
+        p.k_new = k_new; p.v_new = v_new; p.new_stride_b = new_stride_b;
+        p.new_stride_h = new_stride_h; p.pt_w = page_table; p.free_stack = free_stack;
+        p.free_top = free_top; p.sal_init_norm = salience_init == RKV_SAL_NORM;
+        return status_of(launch_fused(p, S(stream)));
+    }
+    st = rkv_append(kv, sal, k_new, v_new, new_stride_b, new_stride_h, 0, 1, kv->num_tokens,
+                    page_table, free_stack, free_top, salience_init, stream);
+    if (st) return st;
     return rkv_decode_fused(q, &grown, sal, decay, one_minus_decay, scale, out, workspace,
                             workspace_bytes, stream);
 }

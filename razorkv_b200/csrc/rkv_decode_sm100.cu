@@ -69,6 +69,10 @@ struct DevArgs {
     float* partials; int* counters; int* err;
     int stages, stage_bytes, tile_bytes, kv_tile_bytes, half_bytes;
     int role[3];   // tensor-map dims 2..4 in stride order: 0 = kv head, 1 = sequence, 2 = page slot
+    // fused append of the token at position N - 1 (k_new == nullptr: none)
+    const void* k_new; const void* v_new; int64_t new_stride_b, new_stride_h;
+    int64_t* pt_w; const int64_t* free_stack; int64_t free_top; int sal_init_norm;
+    void* kpool; void* vpool; int64_t stride_b, stride_h, stride_p, stride_t;
 };
 
 struct SmemTail {             // placed after the stage ring
@@ -80,6 +84,7 @@ struct SmemTail {             // placed after the stage ring
     uint16_t ps[kComputeWarps][8][kTileTokens];   // P (bf16/fp16) per warp: [head][token]
     float alpha[kComputeWarps][8];
     alignas(16) float sal_old[kMaxStages][kComputeWarps][kTileTokens];   // bulk-copied salience rows
+    float new_norm[kMaxStages][kComputeWarps][8];   // ||k_h|| of the appended token, per kv head
     int last;
     int abort;
 };
@@ -210,12 +215,23 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
     for (int i = threadIdx.x; i < kComputeWarps * 8; i += blockDim.x) (&sm.alpha[0][0])[i] = 0.f;
     if (threadIdx.x == 0) sm.abort = 0;
     __syncthreads();
+    // Launched with programmatic stream serialization: everything above overlaps the previous
+    // kernel's tail; from here on global memory written by earlier work is read, so wait for
+    // it.  The merge kernel that follows may be scheduled as soon as SMs free up.
+    grid_dependency_wait();
+    grid_launch_dependents();
 
     const int64_t c = blockIdx.x;
     const int64_t r0 = c * a.W;
     const int64_t r1 = min(a.total, r0 + a.W);
     const int wph = a.wph;
     const int Hkv = a.Hkv;
+    // fused append: the token at position N - 1 is written by this kernel (tile new_tile,
+    // row new_row); when new_row == 0 its page is taken from the free stack here
+    const bool append = a.k_new != nullptr;
+    const int new_tile = (int)((a.N - 1) / kTileTokens);
+    const int new_row = (int)((a.N - 1) % kTileTokens);
+    const bool app_new_page = append && new_row == 0;
 
     // ------------------------------------------------------------------- producer warp
     // The whole warp walks the schedule; lanes fetch the page ids of the next 32 tiles
@@ -249,7 +265,12 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                             win = t;
                             pid = (win + lane < tb1) ? __ldg(ptb + win + lane) : 0;
                         }
-                        const int64_t v = __shfl_sync(0xffffffffu, pid, (int)(t - win));
+                        int64_t v = __shfl_sync(0xffffffffu, pid, (int)(t - win));
+                        if (app_new_page && t == new_tile) {
+                            // the appended token opens a page: take the free stack's top
+                            v = __ldg(a.free_stack + a.free_top - 1);
+                            if (lane == 0) a.pt_w[b * a.pt_stride_b + t] = v;
+                        }
                         ph[s] = (v < 0 || v >= a.num_slots) ? -1 : (int32_t)v;
                     }
                 }
@@ -339,6 +360,47 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                 const uint32_t kb = smem_u32(tbase) + h * kTileTokens * 128;
                 const uint32_t vb = kb + a.kv_tile_bytes;
 
+                // ---- 0. fused append of the token at N - 1 --------------------------------
+                // Copy this kv head's new K and V rows into the staged page (the page in HBM
+                // still holds an older row there) and into the pool page for later steps, and
+                // take ||k|| in the canonical order for the token's initial salience.
+                const bool has_new = append && tile == new_tile;
+                if (has_new) {
+                    const int phys = sm.phys[slot][s];
+                    constexpr int NCH = D / 8;   // 16-byte chunks per row
+                    for (int i = lane; i < 2 * NCH; i += 32) {
+                        const bool isv = i >= NCH;
+                        const int cidx = isv ? i - NCH : i;
+                        const T* src = static_cast<const T*>(isv ? a.v_new : a.k_new) +
+                                       b * a.new_stride_b + (int64_t)h * a.new_stride_h + cidx * 8;
+                        const uint4 w = *reinterpret_cast<const uint4*>(src);
+                        const int hf = cidx >> 3, c8 = cidx & 7;
+                        sts128((isv ? vb : kb) + hf * a.half_bytes + new_row * 128 +
+                                   ((c8 ^ (new_row & 7)) << 4),
+                               w);
+                        if (phys >= 0) {
+                            T* dst = static_cast<T*>(isv ? a.vpool : a.kpool) + b * a.stride_b +
+                                     (int64_t)h * a.stride_h + (int64_t)phys * a.stride_p +
+                                     (int64_t)new_row * a.stride_t + cidx * 8;
+                            *reinterpret_cast<uint4*>(dst) = w;
+                        }
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    uint64_t x = 0ull;
+#pragma unroll
+                    for (int hf = 0; hf < HALVES; ++hf) {
+                        uint64_t kq[4];
+                        unpack8_pairs<T>(lds128(kb + hf * a.half_bytes + new_row * 128 +
+                                                ((j ^ (new_row & 7)) << 4)),
+                                         kq);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) ffma2(x, kq[e], kq[e]);
+                    }
+                    const float nrm = __fsqrt_rn(group8_sum(sum_pair(x)));
+                    if (lane == 0) sm.new_norm[slot][s][h] = nrm;
+                }
+
                 // ---- 1. scores, canonical order -------------------------------------
                 float sc[4];
 #pragma unroll
@@ -402,7 +464,19 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                             if (lane < nv && phys >= 0) {
                                 float* sp = a.sal + (int64_t)phys * a.sal_stride_p + b * a.sal_stride_b + lane;
                                 const float R = key_to_float(key);
-                                const float old = a.sal_bulk ? sm.sal_old[slot][s][lane] : *sp;
+                                float old;
+                                if (has_new && lane == new_row) {
+                                    // initial salience of the appended token (mean ||k_h||)
+                                    old = 1.0f;
+                                    if (a.sal_init_norm) {
+                                        float acc = 0.0f;
+                                        for (int hh = 0; hh < Hkv; ++hh)
+                                            acc = __fadd_rn(acc, sm.new_norm[slot][s][hh]);
+                                        old = __fdiv_rn(acc, (float)Hkv);
+                                    }
+                                } else {
+                                    old = a.sal_bulk ? sm.sal_old[slot][s][lane] : *sp;
+                                }
                                 *sp = __fadd_rn(__fmul_rn(a.decay, old), __fmul_rn(a.omd, R));
                             }
                             sm.red[slot][s][lane] = 0u;
@@ -526,6 +600,8 @@ struct MergeArgs {
 template <typename T, int D>
 __global__ void __launch_bounds__(D)
 merge_kernel(const MergeArgs a) {
+    grid_dependency_wait();   // the partials come from the decode kernel just before
+    grid_launch_dependents();
     constexpr int RS = D + 4;
     const int lane = threadIdx.x & 31;
     const int d = threadIdx.x;
@@ -692,13 +768,34 @@ static cudaError_t launch_t(const FusedParams& f, const Plan& pl, CUtensorMapDat
     a.stages = pl.stages; a.stage_bytes = pl.stage_bytes; a.tile_bytes = pl.tile_bytes;
     a.kv_tile_bytes = pl.kv_tile_bytes; a.half_bytes = pl.half_bytes;
     for (int i = 0; i < 3; ++i) a.role[i] = role[i];
-    kern<<<(unsigned)pl.grid, kThreads, pl.smem_bytes, stream>>>(mk, mv, a);
-    cudaError_t e = counted(cudaGetLastError(), 1);
+    a.k_new = (f.k_new && f.sal && f.attend) ? f.k_new : nullptr;
+    a.v_new = f.v_new; a.new_stride_b = f.new_stride_b; a.new_stride_h = f.new_stride_h;
+    a.pt_w = f.pt_w; a.free_stack = f.free_stack; a.free_top = f.free_top;
+    a.sal_init_norm = f.sal_init_norm;
+    a.kpool = const_cast<void*>(f.k); a.vpool = const_cast<void*>(f.v);
+    a.stride_b = f.stride_b; a.stride_h = f.stride_h; a.stride_p = f.stride_p;
+    a.stride_t = f.stride_t;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)pl.grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = (size_t)pl.smem_bytes;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = counted(cudaLaunchKernelEx(&cfg, kern, mk, mv, a), 1);
     if (e != cudaSuccess || !f.attend) return e;
     MergeArgs m{f.partials, f.out, f.o_stride_b, f.o_stride_h, f.Hq, pl.wph, pl.n_tiles, pl.W,
                 pl.maxc};
-    merge_kernel<T, D><<<(unsigned)(f.B * f.Hq), D, 0, stream>>>(m);
-    return counted(cudaGetLastError(), 1);
+    cudaLaunchConfig_t mcfg{};
+    mcfg.gridDim = dim3((unsigned)(f.B * f.Hq));
+    mcfg.blockDim = dim3(D);
+    mcfg.stream = stream;
+    mcfg.attrs = attr;
+    mcfg.numAttrs = 1;
+    return counted(cudaLaunchKernelEx(&mcfg, merge_kernel<T, D>, m), 1);
 }
 
 }  // namespace sm100

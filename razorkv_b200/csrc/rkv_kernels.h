@@ -82,6 +82,9 @@ struct FusedParams {
     int attend;                                        // 0: score only (no V, no output)
     void* out; int64_t o_stride_b, o_stride_h;
     float* partials; int* counters; int* err;   // workspace body / header (nullptr: score only)
+    // fused append of one new token at position N - 1 (k_new == nullptr: no append)
+    const void* k_new; const void* v_new; int64_t new_stride_b, new_stride_h;
+    int64_t* pt_w; const int64_t* free_stack; int64_t free_top; int sal_init_norm;
 };
 
 cudaError_t launch_score(const ScoreParams& p, cudaStream_t st);

@@ -184,6 +184,16 @@ __device__ __forceinline__ void set_max_regs_dec() {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
+// Programmatic dependent launch: wait until the preceding grid in the stream has completed
+// and its memory is visible (a no-op when the kernel was launched without the attribute),
+// and allow the next grid to be scheduled early.
+__device__ __forceinline__ void grid_dependency_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Named barrier over the compute warps only (the producer warp never joins it).
 __device__ __forceinline__ void compute_barrier(int nthreads) {
     asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
