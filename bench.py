@@ -321,12 +321,8 @@ def main():
     cache = PagedRazorKVCache(cfg, L, max_slots=pool_slots(w, cfg, total_steps, layers))
 
     if world > 1:
-        def reducer(scores):
-            out = torch.empty((world * scores.shape[0], scores.shape[1]), dtype=scores.dtype,
-                              device=scores.device)
-            dist.all_gather_into_tensor(out, scores.contiguous())
-            return out
-        cache.score_reducer = reducer
+        from razorkv_b200.distributed import batch_sharded_score_reducer
+        cache.score_reducer = batch_sharded_score_reducer()
 
     # ---- prefill (untimed)
     t0 = time.time()
@@ -360,14 +356,15 @@ def main():
     for s in range(args.warmup):
         step(s)
     torch.cuda.synchronize()
+    lib = _lib.load()
+    # every rank samples its own GPU's clocks; the samplers start before the barrier so that
+    # no rank enters the timed region while another is still setting up
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.4)
+    timer.prepare(args.steps * len(layers) + 8)
     if world > 1:
         dist.barrier()
-    lib = _lib.load()
-    clocks = ClockSampler(local) if rank == 0 else None
-    if clocks:
-        clocks.start()
-        time.sleep(0.4)
-    timer.prepare(args.steps * len(layers) + 8)
     timer.enabled = True
     launches0 = lib.rkv_launch_count()
     torch.cuda.synchronize()
@@ -388,6 +385,17 @@ def main():
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
+        infos = [None] * world
+        dist.all_gather_object(infos, clock_info)
+        infos = [i for i in infos if i]
+        if infos:
+            clock_info = {
+                "sm_mhz": statistics.median(i["sm_mhz"] for i in infos),
+                "sm_max_mhz": max(i["sm_max_mhz"] for i in infos),
+                "reasons": sorted(set(r for i in infos for r in i["reasons"])),
+                "samples": sum(i["samples"] for i in infos),
+                "gpus": len(infos),
+            }
         dist.barrier()
 
     # ---- end to end: host inputs, public API, outputs back to the host
