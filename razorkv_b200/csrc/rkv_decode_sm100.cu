@@ -6,10 +6,12 @@
 // number of bytes whatever B and N are).  A range that crosses a sequence boundary is
 // processed as one *segment* per sequence.
 //
-// CTA = 8 compute warps + 1 producer warp.
+// CTA = 8 compute warps + 1 producer warp + 1 salience finisher warp (when scoring).
 //   producer : one lane walks the CTA's tiles, reads the page table and issues 5-D TMA tile
 //              loads (128-byte swizzle, no multicast) of K and V for all kv heads of up to
 //              8/Hkv tiles per pipeline stage into an NS-deep shared-memory ring.
+//   finisher : folds the compute warps' per-token maxima over the kv heads, applies the
+//              EWMA and stores the salience; the stage is released once it is done too.
 //   compute  : warp w serves kv head h = w % Hkv of tile slot s = w / Hkv of every stage,
 //              i.e. GQA packing: each K/V page is read from HBM once and used by the G query
 //              heads of its kv head.
@@ -18,9 +20,9 @@
 //   1. computes the 16 x G scores q.k in fp32 on CUDA cores in the canonical order shared
 //      with the CPU oracle (lane j of an 8-lane group owns the 16-byte chunks j, j+8 of the K
 //      row; fused multiply-adds from +0.0f; xor-4/2/1 butterfly), so salience is bit-exact;
-//   2. (score) takes the max over its heads per token and folds it into the per-tile
-//      shared-memory maximum; the last of the Hkv warps of the tile applies
-//      S = fl(fl(d*S) + fl((1-d)*R)) to the 16 tokens' salience in HBM;
+//   2. (score) takes the max over its heads per token and stores it as an ordered key in
+//      shared memory (plain stores, no atomics); the finisher takes the max over the Hkv
+//      keys of each token and applies S = fl(fl(d*S) + fl((1-d)*R)) to its salience in HBM;
 //   3. (attend) runs the online softmax in the log2 domain with warp shuffles, stores the
 //      probabilities as bf16/fp16 and accumulates P.V with mma.sync m16n8k16 (Vt as the A
 //      operand straight from the swizzled stage via ldmatrix.trans, P^T as B).
@@ -78,14 +80,15 @@ struct DevArgs {
 struct SmemTail {             // placed after the stage ring
     uint64_t full[kMaxStages];
     uint64_t empty[kMaxStages];
+    uint64_t scored[kMaxStages];   // every compute thread has stored its resonance keys
     int32_t phys[kMaxStages][kComputeWarps];
+    // per compute warp (tile slot s, kv head h) = warp s * Hkv + h: the token's max score
+    // over the warp's query heads as an ordered key
     uint32_t red[kMaxStages][kComputeWarps][kTileTokens];
-    int32_t redcnt[kMaxStages][kComputeWarps];
     uint16_t ps[kComputeWarps][8][kTileTokens];   // P (bf16/fp16) per warp: [head][token]
     float alpha[kComputeWarps][8];
     alignas(16) float sal_old[kMaxStages][kComputeWarps][kTileTokens];   // bulk-copied salience rows
     float new_norm[kMaxStages][kComputeWarps][8];   // ||k_h|| of the appended token, per kv head
-    int last;
     int abort;
 };
 
@@ -202,14 +205,13 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
     if (threadIdx.x == 0) {
         for (int s = 0; s < NS; ++s) {
             mbar_init(&sm.full[s], 1);
-            mbar_init(&sm.empty[s], kComputeWarps);
+            // a stage is free once every compute warp and, when scoring, the salience
+            // finisher are done with it
+            mbar_init(&sm.empty[s], kComputeWarps + (a.score ? 1 : 0));
+            mbar_init(&sm.scored[s], kComputeThreads);
         }
         fence_mbar_init();
     }
-    for (int i = threadIdx.x; i < kMaxStages * kComputeWarps * kTileTokens; i += blockDim.x)
-        (&sm.red[0][0][0])[i] = 0u;
-    for (int i = threadIdx.x; i < kMaxStages * kComputeWarps; i += blockDim.x)
-        (&sm.redcnt[0][0])[i] = 0;
     for (int i = threadIdx.x; i < kComputeWarps * 8 * kTileTokens; i += blockDim.x)
         (&sm.ps[0][0][0])[i] = 0;
     for (int i = threadIdx.x; i < kComputeWarps * 8; i += blockDim.x) (&sm.alpha[0][0])[i] = 0.f;
@@ -240,6 +242,55 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
     // EWMA update never waits on a global load.
     if (warp >= kComputeWarps) {
         set_max_regs_dec<kProducerRegs>();
+        if (warp == kComputeWarps + 1 && a.score) {
+            // ---- salience finisher --------------------------------------------------------
+            // Folds the compute warps' per-token keys over the kv heads, applies the EWMA
+            // and stores the salience, then releases the stage.  Doing this here keeps the
+            // cross-warp fold off the compute warps' path: they only store their keys.
+            int slot = 0;
+            uint32_t par = 0;
+            for (int64_t pos = r0; pos < r1;) {
+                const int64_t b = pos / a.n_tiles;
+                const int64_t seg_end = min(r1, (b + 1) * a.n_tiles);
+                const int64_t tb0 = pos - b * a.n_tiles, tb1 = seg_end - b * a.n_tiles;
+                for (int64_t t0 = tb0; t0 < tb1; t0 += wph) {
+                    const int ntile = (int)(tb1 - t0 < wph ? tb1 - t0 : wph);
+                    if (mbar_wait(&sm.scored[slot], par, a.err, &sm.abort)) {
+                        for (int i = lane; i < ntile * kTileTokens; i += 32) {
+                            const int s = i / kTileTokens, t = i % kTileTokens;
+                            const int64_t tile = t0 + s;
+                            const int64_t nv = a.N - tile * kTileTokens;
+                            const int phys = sm.phys[slot][s];
+                            if (t >= nv || phys < 0) continue;
+                            uint32_t key = 0u;
+                            for (int hh = 0; hh < Hkv; ++hh) key = max(key, sm.red[slot][s * Hkv + hh][t]);
+                            const float R = key_to_float(key);
+                            float old;
+                            if (append && tile == new_tile && t == new_row) {
+                                // initial salience of the appended token (mean ||k_h||)
+                                old = 1.0f;
+                                if (a.sal_init_norm) {
+                                    float acc = 0.0f;
+                                    for (int hh = 0; hh < Hkv; ++hh)
+                                        acc = __fadd_rn(acc, sm.new_norm[slot][s][hh]);
+                                    old = __fdiv_rn(acc, (float)Hkv);
+                                }
+                            } else {
+                                old = a.sal_bulk ? sm.sal_old[slot][s][t]
+                                                 : a.sal[(int64_t)phys * a.sal_stride_p + b * a.sal_stride_b + t];
+                            }
+                            a.sal[(int64_t)phys * a.sal_stride_p + b * a.sal_stride_b + t] =
+                                __fadd_rn(__fmul_rn(a.decay, old), __fmul_rn(a.omd, R));
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&sm.empty[slot]);
+                    if (++slot == NS) { slot = 0; par ^= 1u; }
+                }
+                pos = seg_end;
+            }
+            return;
+        }
         if (warp != kComputeWarps) return;   // the rest of the producer warpgroup idles out
         if (lane == 0) {
             prefetch_tensormap(&tmk);
@@ -423,7 +474,9 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                     sc[r] = group_transpose_reduce<GP>(part, j);
                 }
 
-                // ---- 2. resonance: max over this warp's heads, folded across kv heads ----
+                // ---- 2. resonance: max over this warp's heads --------------------------
+                // The fold over kv heads, the EWMA and the store are the salience
+                // finisher's; this warp stores one key per token and arrives on scored.
                 if (a.score) {
                     // transpose-max over the 8 lanes of the group: afterwards lane j holds
                     // the max over heads of round rj = 2*bit2(j) + bit1(j), i.e. token 4*rj + g
@@ -449,40 +502,9 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                     key[0] = max(key[0], __shfl_xor_sync(0xffffffffu, key[0], 1));
                     {
                         const int t = 4 * (((j >> 2) & 1) * 2 + ((j >> 1) & 1)) + g;
-                        if ((j & 1) == 0 && t < nv) atomicMax(&sm.red[slot][s][t], key[0]);
+                        if ((j & 1) == 0) sm.red[slot][warp][t] = key[0];
                     }
-                    __threadfence_block();
-                    __syncwarp();
-                    int last = 0;
-                    if (lane == 0) last = atomicAdd(&sm.redcnt[slot][s], 1) == Hkv - 1;
-                    last = __shfl_sync(0xffffffffu, last, 0);
-                    if (last) {
-                        __threadfence_block();
-                        if (lane < kTileTokens) {
-                            const int phys = sm.phys[slot][s];
-                            const uint32_t key = sm.red[slot][s][lane];
-                            if (lane < nv && phys >= 0) {
-                                float* sp = a.sal + (int64_t)phys * a.sal_stride_p + b * a.sal_stride_b + lane;
-                                const float R = key_to_float(key);
-                                float old;
-                                if (has_new && lane == new_row) {
-                                    // initial salience of the appended token (mean ||k_h||)
-                                    old = 1.0f;
-                                    if (a.sal_init_norm) {
-                                        float acc = 0.0f;
-                                        for (int hh = 0; hh < Hkv; ++hh)
-                                            acc = __fadd_rn(acc, sm.new_norm[slot][s][hh]);
-                                        old = __fdiv_rn(acc, (float)Hkv);
-                                    }
-                                } else {
-                                    old = a.sal_bulk ? sm.sal_old[slot][s][lane] : *sp;
-                                }
-                                *sp = __fadd_rn(__fmul_rn(a.decay, old), __fmul_rn(a.omd, R));
-                            }
-                            sm.red[slot][s][lane] = 0u;
-                        }
-                        if (lane == 0) sm.redcnt[slot][s] = 0;
-                    }
+                    mbar_arrive(&sm.scored[slot]);
                 }
 
                 // ---- 3. online softmax + P.V on tensor cores ------------------------------
@@ -552,6 +574,8 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                     }
                     __syncwarp();
                 }
+            } else if (a.score) {
+                mbar_arrive(&sm.scored[slot]);   // no tile in this slot: keep the count whole
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&sm.empty[slot]);
@@ -832,15 +856,19 @@ cudaError_t launch_fused(const FusedParams& p, cudaStream_t st) {
     cudaError_t e;
     if (p.dtype == RKV_BF16) {
         const auto dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-        if (p.D == 128) e = G <= 4 ? launch_t<__nv_bfloat16, 128, 4>(p, pl, dt, st)
+        if (p.D == 128) e = G <= 2 ? launch_t<__nv_bfloat16, 128, 2>(p, pl, dt, st)
+                          : G <= 4 ? launch_t<__nv_bfloat16, 128, 4>(p, pl, dt, st)
                                    : launch_t<__nv_bfloat16, 128, 8>(p, pl, dt, st);
-        else e = G <= 4 ? launch_t<__nv_bfloat16, 64, 4>(p, pl, dt, st)
+        else e = G <= 2 ? launch_t<__nv_bfloat16, 64, 2>(p, pl, dt, st)
+               : G <= 4 ? launch_t<__nv_bfloat16, 64, 4>(p, pl, dt, st)
                         : launch_t<__nv_bfloat16, 64, 8>(p, pl, dt, st);
     } else {
         const auto dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-        if (p.D == 128) e = G <= 4 ? launch_t<__half, 128, 4>(p, pl, dt, st)
+        if (p.D == 128) e = G <= 2 ? launch_t<__half, 128, 2>(p, pl, dt, st)
+                          : G <= 4 ? launch_t<__half, 128, 4>(p, pl, dt, st)
                                    : launch_t<__half, 128, 8>(p, pl, dt, st);
-        else e = G <= 4 ? launch_t<__half, 64, 4>(p, pl, dt, st)
+        else e = G <= 2 ? launch_t<__half, 64, 2>(p, pl, dt, st)
+               : G <= 4 ? launch_t<__half, 64, 4>(p, pl, dt, st)
                         : launch_t<__half, 64, 8>(p, pl, dt, st);
     }
     return e;

@@ -57,6 +57,8 @@ SHAPES = [
     (4, 16, 4, 64, 513),       # head_dim 64
     (1, 8, 8, 128, 16),        # one page, G = 1
     (5, 40, 8, 128, 3),        # fewer tokens than a page
+    (2, 6, 2, 128, 900),       # G = 3: the second query-head slice has one live head
+    (3, 16, 8, 128, 1500),     # G = 2
 ]
 
 
