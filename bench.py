@@ -56,6 +56,8 @@ def parse_args():
                     help="run a single layer of the workload (budget as in the full model); "
                          "a small case for profiling")
     ap.add_argument("--context", type=int, default=0, help="override the prefill length (profiling)")
+    ap.add_argument("--event-every", type=int, default=8,
+                    help="record per-launch CUDA events on every k-th timed step")
     return ap.parse_args()
 
 
@@ -132,12 +134,21 @@ def pool_slots(w, cfg, steps, layers):
 
 
 class KernelTimer:
-    """CUDA events around every decode-kernel launch of decode_step."""
+    """Counts the retained K/V bytes of every decode-kernel launch of decode_step inside the
+    timed region, and records CUDA events around the launches of the sampled steps.
 
-    def __init__(self, torch):
+    An event recorded between two launches ends the programmatic overlap of the second
+    launch's start with the first one's tail, so events go only around the launches of every
+    ``every``-th timed step; the other steps run as a user's would."""
+
+    def __init__(self, torch, every=1):
         self.torch = torch
         self.pairs = []
-        self.enabled = False
+        self.enabled = False      # inside the timed region
+        self.sampling = False     # this step's launches get events
+        self.every = max(1, every)
+        self.all_bytes = 0
+        self.all_launches = 0
         self.pool = []
 
     def prepare(self, n):
@@ -148,6 +159,10 @@ class KernelTimer:
     def before(self, layer, kv_bytes):
         if not self.enabled:
             return
+        self.all_bytes += kv_bytes
+        self.all_launches += 1
+        if not self.sampling:
+            return
         i = len(self.pairs)
         e0, e1 = self.pool[i] if i < len(self.pool) else (
             self.torch.cuda.Event(enable_timing=True), self.torch.cuda.Event(enable_timing=True))
@@ -155,7 +170,7 @@ class KernelTimer:
         self.pairs.append([e0, e1, kv_bytes])
 
     def after(self):
-        if not self.enabled:
+        if not (self.enabled and self.sampling):
             return
         self.pairs[-1][1].record()
 
@@ -337,7 +352,7 @@ def main():
     n_dev_steps = args.warmup + args.steps
     inputs = [{l: decode_inputs(wr, s, l, dev) for l in layers} for s in range(n_dev_steps)]
     outs = {l: torch.empty(B, w.num_q_heads, 1, w.head_dim, dtype=w.dtype, device=dev) for l in layers}
-    timer = KernelTimer(torch)
+    timer = KernelTimer(torch, every=args.event_every)
     cache.launch_observer = timer
 
     single = len(layers) == 1 and layers[0] != 0
@@ -347,6 +362,7 @@ def main():
         cache._seen_tokens = w.context
 
     def step(s):
+        timer.sampling = (s - args.warmup) % timer.every == 0
         if single:
             cache._seen_tokens += 1
         for l in layers:
@@ -362,7 +378,7 @@ def main():
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.4)
-    timer.prepare(args.steps * len(layers) + 8)
+    timer.prepare(-(-args.steps // timer.every) * len(layers) + 8)
     if world > 1:
         dist.barrier()
     timer.enabled = True
@@ -450,7 +466,7 @@ def main():
     peak, peak_kind = peaks()
     achieved = (kern_bytes / n_launch) / ((kern_ms / n_launch) / 1e3) / 1e9 if n_launch else 0.0
     tpb = traffic_per_byte()
-    step_bytes = kern_bytes / max(args.steps, 1)
+    step_bytes = timer.all_bytes / max(args.steps, 1)
     value = world * B * args.steps / (ms / 1e3)
     line = {
         "metric": METRIC,
@@ -475,6 +491,8 @@ def main():
             "frac": achieved / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
             "kernel": "rkv::sm100::decode_kernel (score+attend, and attend-only on compaction steps)",
             "launches": n_launch, "kernel_ms_total": kern_ms,
+            "timed_launches": f"CUDA events around each decode launch of every {timer.every}-th "
+                              f"timed step ({n_launch} of {timer.all_launches} launches)",
             "traffic": (tpb * kern_bytes / n_launch) if (tpb and n_launch) else None,
         },
         "gpu_launches": int(launches),

@@ -80,7 +80,7 @@ struct DevArgs {
 struct SmemTail {             // placed after the stage ring
     uint64_t full[kMaxStages];
     uint64_t empty[kMaxStages];
-    uint64_t scored[kMaxStages];   // every compute thread has stored its resonance keys
+    uint64_t scored[kMaxStages];   // every compute warp has stored its resonance keys
     int32_t phys[kMaxStages][kComputeWarps];
     // per compute warp (tile slot s, kv head h) = warp s * Hkv + h: the token's max score
     // over the warp's query heads as an ordered key
@@ -208,7 +208,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
             // a stage is free once every compute warp and, when scoring, the salience
             // finisher are done with it
             mbar_init(&sm.empty[s], kComputeWarps + (a.score ? 1 : 0));
-            mbar_init(&sm.scored[s], kComputeThreads);
+            mbar_init(&sm.scored[s], kComputeWarps);
         }
         fence_mbar_init();
     }
@@ -216,18 +216,44 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
         (&sm.ps[0][0][0])[i] = 0;
     for (int i = threadIdx.x; i < kComputeWarps * 8; i += blockDim.x) (&sm.alpha[0][0])[i] = 0.f;
     if (threadIdx.x == 0) sm.abort = 0;
-    __syncthreads();
-    // Launched with programmatic stream serialization: everything above overlaps the previous
-    // kernel's tail; from here on global memory written by earlier work is read, so wait for
-    // it.  The merge kernel that follows may be scheduled as soon as SMs free up.
-    grid_dependency_wait();
-    grid_launch_dependents();
 
     const int64_t c = blockIdx.x;
     const int64_t r0 = c * a.W;
     const int64_t r1 = min(a.total, r0 + a.W);
     const int wph = a.wph;
     const int Hkv = a.Hkv;
+
+    // Before the wait on the previous kernel: fetch the tensor maps and warm L2 with the
+    // pages of the first stages.  Page ids read here may be stale (the previous kernel may
+    // still rewrite the table), which only makes a prefetch useless; they bypass L1, and
+    // every load that feeds the computation happens after the wait.
+    if (warp == kComputeWarps && lane == 0) {
+        prefetch_tensormap(&tmk);
+        if (a.attend) prefetch_tensormap(&tmv);
+        if (r0 < r1) {
+            const int64_t b = r0 / a.n_tiles;
+            const int64_t t_begin = r0 - b * a.n_tiles;
+            const int64_t t_seg = min(r1, (b + 1) * a.n_tiles) - b * a.n_tiles;
+            const int64_t t_end = min(t_seg, t_begin + (int64_t)NS * wph);
+            for (int64_t t = t_begin; t < t_end; ++t) {
+                const int64_t v = __ldcg(a.pt + b * a.pt_stride_b + t);
+                if (v < 0 || v >= a.num_slots) continue;
+                int cc[3];
+#pragma unroll
+                for (int k = 0; k < 3; ++k) cc[k] = a.role[k] == 0 ? 0 : a.role[k] == 1 ? (int)b : (int)v;
+                for (int hf = 0; hf < D / 64; ++hf) {
+                    tma_prefetch_l2_5d(&tmk, hf * 64, 0, cc[0], cc[1], cc[2]);
+                    if (a.attend) tma_prefetch_l2_5d(&tmv, hf * 64, 0, cc[0], cc[1], cc[2]);
+                }
+            }
+        }
+    }
+    __syncthreads();
+    // Launched with programmatic stream serialization: everything above overlaps the previous
+    // kernel's tail; from here on global memory written by earlier work is read, so wait for
+    // it.  The merge kernel that follows may be scheduled as soon as SMs free up.
+    grid_dependency_wait();
+    grid_launch_dependents();
     // fused append: the token at position N - 1 is written by this kernel (tile new_tile,
     // row new_row); when new_row == 0 its page is taken from the free stack here
     const bool append = a.k_new != nullptr;
@@ -292,10 +318,6 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
             return;
         }
         if (warp != kComputeWarps) return;   // the rest of the producer warpgroup idles out
-        if (lane == 0) {
-            prefetch_tensormap(&tmk);
-            if (a.attend) prefetch_tensormap(&tmv);
-        }
         int slot = 0;
         uint32_t par = 0;
         for (int64_t pos = r0; pos < r1;) {
@@ -504,7 +526,8 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                         const int t = 4 * (((j >> 2) & 1) * 2 + ((j >> 1) & 1)) + g;
                         if ((j & 1) == 0) sm.red[slot][warp][t] = key[0];
                     }
-                    mbar_arrive(&sm.scored[slot]);
+                    __syncwarp();   // orders the lanes' key stores before lane 0's release
+                    if (lane == 0) mbar_arrive(&sm.scored[slot]);
                 }
 
                 // ---- 3. online softmax + P.V on tensor cores ------------------------------
@@ -575,7 +598,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                     __syncwarp();
                 }
             } else if (a.score) {
-                mbar_arrive(&sm.scored[slot]);   // no tile in this slot: keep the count whole
+                if (lane == 0) mbar_arrive(&sm.scored[slot]);   // no tile in this slot: keep the count whole
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&sm.empty[slot]);
@@ -624,8 +647,10 @@ struct MergeArgs {
 template <typename T, int D>
 __global__ void __launch_bounds__(D)
 merge_kernel(const MergeArgs a) {
-    grid_dependency_wait();   // the partials come from the decode kernel just before
+    // the next decode kernel may start its prologue now; it waits for this grid to finish
+    // before it touches anything this grid reads
     grid_launch_dependents();
+    grid_dependency_wait();   // the partials come from the decode kernel just before
     constexpr int RS = D + 4;
     const int lane = threadIdx.x & 31;
     const int d = threadIdx.x;

@@ -81,6 +81,16 @@ __device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, u
         : "memory");
 }
 
+// The same 5-D tile brought into L2 only (a hint: no shared memory, no completion).
+__device__ __forceinline__ void tma_prefetch_l2_5d(const CUtensorMap* map, int c0, int c1, int c2,
+                                                   int c3, int c4) {
+    asm volatile(
+        "cp.async.bulk.prefetch.tensor.5d.L2.global.tile [%0, {%1, %2, %3, %4, %5}];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+        : "memory");
+}
+
 // Untiled bulk copy global -> shared (no multicast); both addresses 16-byte aligned, size a
 // multiple of 16.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
