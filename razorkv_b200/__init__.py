@@ -4,6 +4,7 @@ Public surface (names as in the reference package ``razorkv``):
 
 * ``RazorConfig``                              razorkv/config.py
 * ``PagedRazorKVCache`` (alias ``RazorKVCache``) razorkv/cache.py
+* ``RazorEngine`` (HF model patcher; paged attention interface) razorkv/engine.py
 * ``kernels``: ``triton_paged_sparse_attention``, ``compacted_paged_sdpa``,
   ``compute_page_salience_pool``, ``is_triton_available``   razorkv/kernels/
 
@@ -12,7 +13,8 @@ use; build it with ``python -m razorkv_b200.build``.
 """
 
 from .config import RazorConfig
-from .cache import PagedRazorKVCache, RazorKVCache, RazorLayerState
+from .cache import PagedKV, PagedRazorKVCache, RazorKVCache, RazorLayerState
+from .engine import RazorEngine
 from . import kernels
 from .kernels import (
     compacted_paged_sdpa,
@@ -29,6 +31,8 @@ __all__ = [
     "PagedRazorKVCache",
     "RazorKVCache",
     "RazorLayerState",
+    "PagedKV",
+    "RazorEngine",
     "kernels",
     "compacted_paged_sdpa",
     "compute_page_salience_pool",

@@ -87,6 +87,33 @@ class RazorLayerState:
         self.cumulative_length = max(0, self.cumulative_length - tokens_to_remove)
 
 
+class PagedKV:
+    """The K (which=0) or V (1) of one layer as ``update`` returns it on decode steps when
+    ``return_handles`` is set: nothing is gathered; ``materialize()`` gives the contiguous
+    ``[B, Hkv, N, D]`` tensor the reference would have returned."""
+
+    __slots__ = ("cache", "layer", "which")
+
+    def __init__(self, cache: "PagedRazorKVCache", layer: int, which: int):
+        self.cache, self.layer, self.which = cache, layer, which
+
+    @property
+    def shape(self) -> torch.Size:
+        c = self.cache
+        return torch.Size((c._B, c._Hkv, c._n[self.layer], c._D))
+
+    @property
+    def dtype(self) -> torch.dtype:
+        return self.cache._dtype
+
+    @property
+    def device(self) -> torch.device:
+        return self.cache._device
+
+    def materialize(self) -> torch.Tensor:
+        return self.cache._materialize(self.layer, self.which)
+
+
 class _LayerList(list):
     """List-like view whose items materialise one layer's K, V or salience."""
 
@@ -141,7 +168,9 @@ class PagedRazorKVCache(BaseCacheClass):
         self.score_reducer: Optional[Callable[[torch.Tensor], torch.Tensor]] = None
         self.record_margins = False
         self.margins: List[Tuple[int, torch.Tensor]] = []
-        self.return_views = False
+        # decode steps of ``update`` return PagedKV handles instead of gathered K/V; the
+        # engine's attention function then reads the pool directly
+        self.return_handles = False
         # optional observer with before(layer, kv_bytes) / after() around every attention
         # launch of decode_step (used to time the decode kernel inside a running step)
         self.launch_observer = None
@@ -483,8 +512,8 @@ class PagedRazorKVCache(BaseCacheClass):
             return ret
         if cur > budget + self.config.page_size:
             self._evict_layer(layer_idx, budget)
-        if self.return_views:
-            return self._k, self._v
+        if self.return_handles:
+            return PagedKV(self, layer_idx, 0), PagedKV(self, layer_idx, 1)
         return self._materialize(layer_idx, 0), self._materialize(layer_idx, 1)
 
     def _budget(self, layer_idx: int) -> int:
