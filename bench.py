@@ -56,6 +56,9 @@ def parse_args():
                     help="run a single layer of the workload (budget as in the full model); "
                          "a small case for profiling")
     ap.add_argument("--context", type=int, default=0, help="override the prefill length (profiling)")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="time K evenly spaced layers of the model only (for caches larger "
+                         "than one GPU's memory); the JSON config records the subset")
     ap.add_argument("--event-every", type=int, default=8,
                     help="record per-launch CUDA events on every k-th timed step")
     return ap.parse_args()
@@ -331,7 +334,13 @@ def main():
     wr = w.scaled(seed=w.seed + 1000 * rank)
     cfg = w.razor_config()
     L, B = w.num_layers, w.batch
-    layers = [args.only_layer] if args.only_layer >= 0 else list(range(L))
+    if args.only_layer >= 0:
+        layers = [args.only_layer]
+    elif 0 < args.layers < L:
+        layers = sorted({round(i * (L - 1) / (args.layers - 1)) for i in range(args.layers)}) \
+            if args.layers > 1 else [0]
+    else:
+        layers = list(range(L))
     total_steps = args.warmup + args.steps + args.e2e_steps
     cache = PagedRazorKVCache(cfg, L, max_slots=pool_slots(w, cfg, total_steps, layers))
 
@@ -481,7 +490,9 @@ def main():
         "vs_baseline": None,
         "dtype": "bf16" if w.dtype == torch.bfloat16 else "fp32",
         "data": "synthetic: seeded N(0,1) K/V/q, 1% planted query-aligned pages per head",
-        "config": workload_config(w, world),
+        "config": dict(workload_config(w, world), **({} if len(layers) == L else {
+            "layer_subset": f"{len(layers)} of {L} layers ({layers[0]}..{layers[-1]}, evenly "
+                            f"spaced); tokens/s counts the timed layers only"})),
         "impl": "b200",
         "tokens_per_s_per_gpu": value / world,
         "retained_kv_gb_per_step": step_bytes / 1e9,

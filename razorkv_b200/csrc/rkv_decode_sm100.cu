@@ -251,9 +251,10 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
     __syncthreads();
     // Launched with programmatic stream serialization: everything above overlaps the previous
     // kernel's tail; from here on global memory written by earlier work is read, so wait for
-    // it.  The merge kernel that follows may be scheduled as soon as SMs free up.
+    // it.  This kernel never triggers its dependents early: the merge grid then launches only
+    // as CTAs exit and spreads over the whole GPU (triggered early, its CTAs piled onto the
+    // few SMs the decode grid leaves free and the merge ran on one or two SMs).
     grid_dependency_wait();
-    grid_launch_dependents();
     // fused append: the token at position N - 1 is written by this kernel (tile new_tile,
     // row new_row); when new_row == 0 its page is taken from the free stack here
     const bool append = a.k_new != nullptr;
@@ -636,33 +637,42 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
     }
 }
 
-// Log-sum-exp merge of the per-warp partials: one CTA per (sequence, query head), one lane
-// per output dimension; every partial's (m, l, acc[d]) is loaded at once (no dependent
-// round-trips), weights 2^(m_p - M) go through shuffles.
+// Log-sum-exp merge of the per-warp partials: one CTA per (sequence, query head) of
+// kMergeGroups x D threads.  Group g folds its share of the partials with one lane per
+// output dimension (every partial's (m, l, acc[d]) of a 32-partial chunk is loaded at once;
+// the weights 2^(m_p - M) go through shuffles); the groups then combine in shared memory.
+// Splitting the partials over groups bounds the chain of dependent L2 round trips when one
+// sequence has hundreds of partials (batch 1).
+constexpr int kMergeGroups = 4;
+
 struct MergeArgs {
     const float* partials; void* out; int64_t o_stride_b, o_stride_h;
     int Hq, wph; int64_t n_tiles, W, maxc;
 };
 
 template <typename T, int D>
-__global__ void __launch_bounds__(D)
+__global__ void __launch_bounds__(kMergeGroups * D)
 merge_kernel(const MergeArgs a) {
     // the next decode kernel may start its prologue now; it waits for this grid to finish
     // before it touches anything this grid reads
     grid_launch_dependents();
     grid_dependency_wait();   // the partials come from the decode kernel just before
     constexpr int RS = D + 4;
+    __shared__ float s_o[kMergeGroups][D];
+    __shared__ float s_m[kMergeGroups], s_l[kMergeGroups];
     const int lane = threadIdx.x & 31;
-    const int d = threadIdx.x;
+    const int grp = threadIdx.x / D;
+    const int d = threadIdx.x % D;
     const int64_t b = blockIdx.x / a.Hq;
     const int hq = blockIdx.x % a.Hq;
     const int64_t cfirst = (b * a.n_tiles) / a.W;
     const int64_t clast = ((b + 1) * a.n_tiles - 1) / a.W;
     const int np = (int)(clast - cfirst + 1) * a.wph;
+    // group g takes whole 32-partial chunks g, g + G, g + 2G, ...
     const float* pb = a.partials + ((b * a.maxc * a.wph) * a.Hq + hq) * (int64_t)RS;
     const int64_t pstride = (int64_t)a.Hq * RS;
     float M = -INFINITY, O = 0.f, L = 0.f;
-    for (int p0 = 0; p0 < np; p0 += 32) {
+    for (int p0 = grp * 32; p0 < np; p0 += kMergeGroups * 32) {
         const int n = min(32, np - p0);
         // lane p holds the stats of partial p0 + p
         const float mp = lane < n ? __ldcg(pb + (p0 + lane) * pstride + D) : -INFINITY;
@@ -687,8 +697,24 @@ merge_kernel(const MergeArgs a) {
         L = L * r + Lc;
         M = Mn;
     }
+    s_o[grp][d] = O;
+    if (d == 0) { s_m[grp] = M; s_l[grp] = L; }
+    __syncthreads();
+    if (grp != 0) return;
+    float Mt = -INFINITY;
+#pragma unroll
+    for (int g = 0; g < kMergeGroups; ++g) Mt = fmaxf(Mt, s_m[g]);
+    float Ot = 0.f, Lt = 0.f;
+    if (Mt != -INFINITY) {
+#pragma unroll
+        for (int g = 0; g < kMergeGroups; ++g) {
+            const float w = s_m[g] == -INFINITY ? 0.f : ex2(s_m[g] - Mt);
+            Ot += s_o[g][d] * w;
+            Lt += s_l[g] * w;
+        }
+    }
     T* ob = static_cast<T*>(a.out) + b * a.o_stride_b + (int64_t)hq * a.o_stride_h;
-    ob[d] = from_f<T>(L > 0.f ? O / L : 0.f);
+    ob[d] = from_f<T>(Lt > 0.f ? Ot / Lt : 0.f);
 }
 
 // ------------------------------------------------------------------------------ host side
@@ -840,7 +866,7 @@ static cudaError_t launch_t(const FusedParams& f, const Plan& pl, CUtensorMapDat
                 pl.maxc};
     cudaLaunchConfig_t mcfg{};
     mcfg.gridDim = dim3((unsigned)(f.B * f.Hq));
-    mcfg.blockDim = dim3(D);
+    mcfg.blockDim = dim3(kMergeGroups * D);
     mcfg.stream = stream;
     mcfg.attrs = attr;
     mcfg.numAttrs = 1;
