@@ -19,6 +19,9 @@
  *   rkv_score                 razorkv/cache.py:249-287 (update_salience_with_query)
  *   rkv_decode_fused          razorkv/cache.py:392-393 followed by the attention call of a
  *                             non-compacting decode step (score and attend in one K pass)
+ *   rkv_decode_scored         razorkv/engine.py:119-126 (the q_proj hook's
+ *                             update_salience_with_query with the pre-RoPE query, before the
+ *                             layer's update) and the layer's attention after it, in one K pass
  *   rkv_page_scores           razorkv/cache.py:322-331 (haystack page max-pool)
  *   rkv_select_pages          razorkv/cache.py:333-341 (batch mean, top-k, ascending sort)
  *   rkv_compact_pages         razorkv/cache.py:343-359 when the sink is page aligned
@@ -185,6 +188,18 @@ int rkv_append_decode(const rkv_kv_layout* kv, const rkv_salience* sal, const vo
                       int salience_init, const rkv_query* q, float decay, float one_minus_decay,
                       float scale, const rkv_output* out, void* workspace, size_t workspace_bytes,
                       void* stream);
+
+/* The HF decode step of the hooked model in one pass over K: the salience of the tokens
+ * before score_tokens is updated as by rkv_score (ewma = 1) with q_score -- the q_proj hook's
+ * pre-RoPE query, which scores the cache before the layer appends its new token -- and the
+ * output is the attention of q_attn (the post-RoPE query) over all kv->num_tokens tokens, as
+ * rkv_decode_attention with causal = 0.  Tokens at or past score_tokens keep their salience.
+ * 0 <= score_tokens <= kv->num_tokens; q_score and q_attn have the same heads, q_len 1. */
+size_t rkv_decode_scored_workspace_size(const rkv_query* q_attn, const rkv_kv_layout* kv);
+int rkv_decode_scored(const rkv_query* q_score, const rkv_query* q_attn, const rkv_kv_layout* kv,
+                      const rkv_salience* sal, int64_t score_tokens, float decay,
+                      float one_minus_decay, float scale, const rkv_output* out,
+                      void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- cache: selection --------------------------------------------------------------------
  * scores[b, p] = max over i < sel_page_size of S(b, first_token + p*sel_page_size + i),

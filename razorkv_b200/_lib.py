@@ -78,6 +78,9 @@ _SIGNATURES = {
     "rkv_append_decode": (ctypes.c_int, [P(KVLayout), P(Salience), c_vp, c_vp, c_i64, c_i64,
                                          c_vp, c_vp, c_i64, ctypes.c_int, P(Query), c_f32, c_f32,
                                          c_f32, P(Output), c_vp, c_sz, c_vp]),
+    "rkv_decode_scored_workspace_size": (c_sz, [P(Query), P(KVLayout)]),
+    "rkv_decode_scored": (ctypes.c_int, [P(Query), P(Query), P(KVLayout), P(Salience), c_i64,
+                                         c_f32, c_f32, c_f32, P(Output), c_vp, c_sz, c_vp]),
     "rkv_page_scores": (ctypes.c_int, [P(KVLayout), P(Salience), c_i64, c_i64, c_i64, c_vp,
                                        c_vp]),
     "rkv_select_pages_workspace_size": (c_sz, [c_i64]),

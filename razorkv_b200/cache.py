@@ -171,6 +171,9 @@ class PagedRazorKVCache(BaseCacheClass):
         # decode steps of ``update`` return PagedKV handles instead of gathered K/V; the
         # engine's attention function then reads the pool directly
         self.return_handles = False
+        # HF hook path with return_handles: the q_proj hook's pre-RoPE query of a decode step
+        # is kept here (layer -> (q, tokens scored)) and scored by the attention pass
+        self._pending: Dict[int, Tuple[torch.Tensor, int]] = {}
         # optional observer with before(layer, kv_bytes) / after() around every attention
         # launch of decode_step (used to time the decode kernel inside a running step)
         self.launch_observer = None
@@ -383,7 +386,11 @@ class PagedRazorKVCache(BaseCacheClass):
 
     # ----------------------------------------------------------------------------- scoring
     def update_salience_with_query(self, query_states: torch.Tensor, layer_idx: int):
-        """razorkv/cache.py:249-287 on the pool (scores every retained token)."""
+        """razorkv/cache.py:249-287 on the pool (scores every retained token).
+
+        With ``return_handles`` set (the engine's paged attention), a single-row query is not
+        scored here: it is kept and scored, over the same tokens, by the layer's attention
+        pass of this step (``rkv_decode_scored``), which reads K once for both."""
         if layer_idx >= len(self._n) or self._n[layer_idx] is None:
             return
         require_cuda(query_states)
@@ -392,17 +399,33 @@ class PagedRazorKVCache(BaseCacheClass):
             q = q.contiguous()
         if q.shape[1] % self._Hkv:
             raise ValueError("query heads must be a multiple of the cache's kv heads")
+        self._flush_pending(layer_idx)
+        if self.return_handles and q.shape[2] == 1 and q.dtype == self._dtype:
+            self._pending[layer_idx] = (q, self._n[layer_idx])
+            return
+        self._score(q, layer_idx, self._n[layer_idx])
+
+    def _score(self, q: torch.Tensor, layer_idx: int, n_tokens: int):
         lib = _lib.load()
         decay = self.config.salience_decay
         st = lib.rkv_score(Query(q.data_ptr(), dtype_code(q.dtype), q.shape[1], q.shape[2],
                                  q.stride(0), q.stride(1), q.stride(2)),
-                           self._layout(layer_idx), self._salience(), float(decay),
+                           self._layout(layer_idx, n_tokens), self._salience(), float(decay),
                            float(1.0 - decay), 1, self._stream())
         check(st, "rkv_score")
+
+    def _flush_pending(self, layer_idx: Optional[int] = None):
+        """Score a kept hook query now (before anything else reads or reshapes the layer)."""
+        layers = list(self._pending) if layer_idx is None else [layer_idx]
+        for l in layers:
+            item = self._pending.pop(l, None)
+            if item is not None:
+                self._score(item[0], l, item[1])
 
     # -------------------------------------------------------------------------- compaction
     def _evict_layer(self, layer_idx: int, target_budget: int):
         """razorkv/cache.py:289-359 on the pool."""
+        self._flush_pending(layer_idx)
         N = self._n[layer_idx]
         if N <= target_budget:
             return
@@ -662,7 +685,10 @@ class PagedRazorKVCache(BaseCacheClass):
 
     def attention(self, query_states: torch.Tensor, layer_idx: int,
                   scaling: Optional[float] = None, is_causal: bool = False) -> torch.Tensor:
-        """Attention of query_states [B, Hq, QL, D] over the retained cache of one layer."""
+        """Attention of query_states [B, Hq, QL, D] over the retained cache of one layer.
+
+        A hook query kept for this layer (see ``update_salience_with_query``) is scored in
+        the same pass over K (``rkv_decode_scored``)."""
         lib = _lib.load()
         q = query_states if query_states.stride(-1) == 1 else query_states.contiguous()
         B, Hq, QL, D = q.shape
@@ -671,6 +697,22 @@ class PagedRazorKVCache(BaseCacheClass):
         os_ = Output(out.data_ptr(), dtype_code(out.dtype), 0, out.stride(0), out.stride(1),
                      out.stride(2))
         lay = self._layout(layer_idx)
+        pending = self._pending.pop(layer_idx, None)
+        if pending is not None:
+            if QL != 1 or is_causal or pending[0].shape[1] != Hq:
+                self._score(pending[0], layer_idx, pending[1])
+            else:
+                qp = pending[0]
+                qps = Query(qp.data_ptr(), dtype_code(qp.dtype), Hq, 1, qp.stride(0),
+                            qp.stride(1), qp.stride(2))
+                decay = self.config.salience_decay
+                ws = Workspace.get(self._device, lib.rkv_decode_scored_workspace_size(qs, lay))
+                st = lib.rkv_decode_scored(qps, qs, lay, self._salience(), pending[1],
+                                           float(decay), float(1.0 - decay),
+                                           float(scaling) if scaling else 0.0, os_,
+                                           ws.data_ptr(), ws.numel(), self._stream())
+                check(st, "rkv_decode_scored")
+                return out
         ws = Workspace.get(self._device, lib.rkv_decode_attention_workspace_size(qs, lay))
         st = lib.rkv_decode_attention(qs, lay, float(scaling) if scaling else 0.0,
                                       1 if (is_causal and QL > 1) else 0, os_, ws.data_ptr(),
@@ -683,6 +725,8 @@ class PagedRazorKVCache(BaseCacheClass):
         """Contiguous [B, Hkv, N, D] K (which=0) / V (1) or [B, N] fp32 salience (2)."""
         if layer_idx >= len(self._n) or self._n[layer_idx] is None:
             return None
+        if which == 2:
+            self._flush_pending(layer_idx)
         lib = _lib.load()
         N = self._n[layer_idx]
         lay = self._layout(layer_idx)
@@ -722,6 +766,7 @@ class PagedRazorKVCache(BaseCacheClass):
         """razorkv/cache.py:177-188: drop the most recent tokens of every layer."""
         if tokens_to_remove <= 0:
             return
+        self._flush_pending()
         for l in range(len(self._n)):
             if self._n[l] is not None:
                 self._crop_layer(l, tokens_to_remove)
@@ -730,6 +775,7 @@ class PagedRazorKVCache(BaseCacheClass):
 
     def reset(self) -> None:
         """razorkv/cache.py:190-196."""
+        self._pending.clear()
         self._n.clear()
         self._pt.clear()
         self._layers.clear()
@@ -740,6 +786,7 @@ class PagedRazorKVCache(BaseCacheClass):
             self._free_top = self._slots
 
     def _reindex_batch(self, index: torch.Tensor):
+        self._flush_pending()
         idx = index.to(self._device)
         self._k = self._k.index_select(1, idx).contiguous()
         self._v = self._v.index_select(1, idx).contiguous()

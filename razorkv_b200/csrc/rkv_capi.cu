@@ -254,6 +254,40 @@ int rkv_decode_fused(const rkv_query* q, const rkv_kv_layout* kv, const rkv_sali
     return rkv_decode_attention(q, kv, scale, 0, out, workspace, workspace_bytes, stream);
 }
 
+size_t rkv_decode_scored_workspace_size(const rkv_query* q_attn, const rkv_kv_layout* kv) {
+    return rkv_decode_attention_workspace_size(q_attn, kv);
+}
+
+int rkv_decode_scored(const rkv_query* q_score, const rkv_query* q_attn, const rkv_kv_layout* kv,
+                      const rkv_salience* sal, int64_t score_tokens, float decay,
+                      float one_minus_decay, float scale, const rkv_output* out,
+                      void* workspace, size_t workspace_bytes, void* stream) {
+    int st = check_kv(kv, true);
+    if (st) return st;
+    if ((st = check_q(q_score, kv)) || (st = check_q(q_attn, kv))) return st;
+    if (!sal || !sal->s || !out || !out->out) return RKV_ERR_INVALID_ARGUMENT;
+    if (q_score->q_len != 1 || q_attn->q_len != 1) return RKV_ERR_UNSUPPORTED;
+    if (q_score->num_heads != q_attn->num_heads) return RKV_ERR_INVALID_ARGUMENT;
+    if (score_tokens < 0 || score_tokens > kv->num_tokens) return RKV_ERR_INVALID_ARGUMENT;
+    if (kv->batch == 0) return RKV_OK;
+    if (workspace_bytes < rkv_decode_scored_workspace_size(q_attn, kv) || !workspace)
+        return RKV_ERR_WORKSPACE_TOO_SMALL;
+    if (kv->num_tokens > 0 && fast_ok(q_attn, kv, true) && q_score->dtype == q_attn->dtype) {
+        FusedParams p = fused_params(q_score, kv, sal, decay, one_minus_decay, scale, out);
+        p.q2 = q_attn->q; p.q2_stride_b = q_attn->stride_b; p.q2_stride_h = q_attn->stride_h;
+        p.has_score_n = 1; p.score_n = score_tokens;
+        p.partials = ws_body(workspace); p.counters = ws_counters(workspace); p.err = ws_err(workspace);
+        return status_of(launch_fused(p, S(stream)));
+    }
+    // shapes outside the fused kernel: score the first score_tokens tokens, then attend
+    if (score_tokens > 0) {
+        rkv_kv_layout scored = *kv;
+        scored.num_tokens = score_tokens;
+        if ((st = rkv_score(q_score, &scored, sal, decay, one_minus_decay, 1, stream))) return st;
+    }
+    return rkv_decode_attention(q_attn, kv, scale, 0, out, workspace, workspace_bytes, stream);
+}
+
 int rkv_append_decode(const rkv_kv_layout* kv, const rkv_salience* sal, const void* k_new,
                       const void* v_new, int64_t new_stride_b, int64_t new_stride_h,
                       int64_t* page_table, const int64_t* free_stack, int64_t free_top,

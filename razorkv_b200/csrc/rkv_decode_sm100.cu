@@ -75,6 +75,10 @@ struct DevArgs {
     const void* k_new; const void* v_new; int64_t new_stride_b, new_stride_h;
     int64_t* pt_w; const int64_t* free_stack; int64_t free_top; int sal_init_norm;
     void* kpool; void* vpool; int64_t stride_b, stride_h, stride_p, stride_t;
+    // MODE 1 / 2: attention query (tensor-core logits) and its log2-domain logit scale;
+    // tokens at or past score_n keep their salience (MODE 2 scores the tokens before it)
+    const void* q2; int64_t q2_stride_b, q2_stride_h;
+    float attn_log2; int64_t score_n;
 };
 
 struct SmemTail {             // placed after the stage ring
@@ -149,6 +153,13 @@ __device__ __forceinline__ void unpack8_pairs<__half>(uint4 w, uint64_t* p) {
     }
 }
 
+// Two 16-bit elements as one 32-bit mma operand register (lo in the low half).
+template <typename T>
+__device__ __forceinline__ uint32_t pack_elems(T lo, T hi) {
+    return (uint32_t)*reinterpret_cast<const uint16_t*>(&lo) |
+           ((uint32_t)*reinterpret_cast<const uint16_t*>(&hi) << 16);
+}
+
 template <typename T>
 __device__ __forceinline__ uint16_t to_bits(float x) {
     T v = from_f<T>(x);
@@ -186,7 +197,12 @@ __device__ __forceinline__ int head_of_lane(int j) {
     return GP == 8 ? j : GP == 4 ? (j >> 1) : GP == 2 ? (j >> 2) : 0;
 }
 
-template <typename T, int D, int GP>
+// MODE 0: one query; its canonical-order scores give the resonance and the attention logits.
+// MODE 1: attention only; the logits come from mma.sync (K tile x q^T, fp32 accumulate).
+// MODE 2: two queries: the canonical-order scores of q (resonance, tokens before score_n)
+//         and the mma.sync logits of q2 (attention over all tokens) -- the HF hook path,
+//         where the hook scores with the pre-RoPE query and attention uses the post-RoPE one.
+template <typename T, int D, int GP, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
 decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
               const DevArgs a) {
@@ -289,6 +305,21 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                             const int64_t nv = a.N - tile * kTileTokens;
                             const int phys = sm.phys[slot][s];
                             if (t >= nv || phys < 0) continue;
+                            if (tile * kTileTokens + t >= a.score_n) {
+                                // not scored this step; only a token appended here gets its
+                                // initial salience
+                                if (append && tile == new_tile && t == new_row) {
+                                    float init = 1.0f;
+                                    if (a.sal_init_norm) {
+                                        float acc = 0.0f;
+                                        for (int hh = 0; hh < Hkv; ++hh)
+                                            acc = __fadd_rn(acc, sm.new_norm[slot][s][hh]);
+                                        init = __fdiv_rn(acc, (float)Hkv);
+                                    }
+                                    a.sal[(int64_t)phys * a.sal_stride_p + b * a.sal_stride_b + t] = init;
+                                }
+                                continue;
+                            }
                             uint32_t key = 0u;
                             for (int hh = 0; hh < Hkv; ++hh) key = max(key, sm.red[slot][s * Hkv + hh][t]);
                             const float R = key_to_float(key);
@@ -397,7 +428,8 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
     const bool head_writer = (j & ((8 / GP) - 1)) == 0;   // one lane per head in each group
     const uint32_t ps_base = smem_u32(&sm.ps[warp][0][0]);
 
-    uint64_t qreg[GP][EPL / 2];   // fl(q * scale) as (even, odd) element pairs
+    uint64_t qreg[GP][EPL / 2];   // MODE 0 / 2: fl(q * scale) as (even, odd) element pairs
+    uint32_t qf[D / 16][2];       // MODE 1 / 2: q2^T as mma B fragments (bf16 / fp16 pairs)
     float acc[MT][4];
     int slot = 0;
     uint32_t par = 0;
@@ -406,20 +438,37 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
         const int64_t seg_end = min(r1, (b + 1) * a.n_tiles);
         const int64_t tb0 = pos - b * a.n_tiles, tb1 = seg_end - b * a.n_tiles;
 
-        // fl(q * scale) for this lane's K elements: chunk j of every 64-element half
-        const T* qb = static_cast<const T*>(a.q) + b * a.q_stride_b;
+        if constexpr (MODE != 1) {
+            // fl(q * scale) for this lane's K elements: chunk j of every 64-element half
+            const T* qb = static_cast<const T*>(a.q) + b * a.q_stride_b;
 #pragma unroll
-        for (int i = 0; i < GP; ++i) {
+            for (int i = 0; i < GP; ++i) {
 #pragma unroll
-            for (int e = 0; e < EPL; e += 2) {
-                const int dim = (e / 8) * 64 + 8 * j + (e % 8);
-                const T* qr = qb + (int64_t)(h * G + i) * a.q_stride_h + dim;
-                const float lo = i < G ? __fmul_rn(to_f<T>(qr[0]), a.scale_r) : 0.0f;
-                const float hi = i < G ? __fmul_rn(to_f<T>(qr[1]), a.scale_r) : 0.0f;
-                qreg[i][e / 2] = pack2(lo, hi);
+                for (int e = 0; e < EPL; e += 2) {
+                    const int dim = (e / 8) * 64 + 8 * j + (e % 8);
+                    const T* qr = qb + (int64_t)(h * G + i) * a.q_stride_h + dim;
+                    const float lo = i < G ? __fmul_rn(to_f<T>(qr[0]), a.scale_r) : 0.0f;
+                    const float hi = i < G ? __fmul_rn(to_f<T>(qr[1]), a.scale_r) : 0.0f;
+                    qreg[i][e / 2] = pack2(lo, hi);
+                }
             }
         }
-        float m_run = -INFINITY, l_run = 0.0f;
+        if constexpr (MODE != 0) {
+            // B = q2^T (dims x heads): lane holds head lane/4, dims 16kk + 2(lane%4) + {0,1}
+            // (b0) and the same + 8 (b1); heads past G are zero
+            const int n = lane >> 2;
+            const T* qr = static_cast<const T*>(a.q2) + b * a.q2_stride_b + (int64_t)(h * G + n) * a.q2_stride_h;
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+                const int d0 = kk * 16 + 2 * (lane & 3);
+                qf[kk][0] = n < G ? pack_elems<T>(qr[d0], qr[d0 + 1]) : 0u;
+                qf[kk][1] = n < G ? pack_elems<T>(qr[d0 + 8], qr[d0 + 9]) : 0u;
+            }
+        }
+        float m_run = -INFINITY, l_run = 0.0f;   // MODE 0: running max / sum of head hl
+        // MODE 1 / 2: the same for heads nA = 2(lane % 4) and nB = nA + 1 (the accumulator's
+        // columns of this lane)
+        float mrA = -INFINITY, mrB = -INFINITY, lrA = 0.0f, lrB = 0.0f;
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -475,8 +524,9 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                     if (lane == 0) sm.new_norm[slot][s][h] = nrm;
                 }
 
-                // ---- 1. scores, canonical order -------------------------------------
-                float sc[4];
+                // ---- 1. scores, canonical order (MODE 0: also the logits) ----------------
+                float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                if constexpr (MODE != 1) {
 #pragma unroll
                 for (int r = 0; r < 4; ++r) {
                     const int t = 4 * r + g;
@@ -496,11 +546,12 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                     }
                     sc[r] = group_transpose_reduce<GP>(part, j);
                 }
+                }
 
                 // ---- 2. resonance: max over this warp's heads --------------------------
                 // The fold over kv heads, the EWMA and the store are the salience
                 // finisher's; this warp stores one key per token and arrives on scored.
-                if (a.score) {
+                if (MODE != 1 && a.score) {
                     // transpose-max over the 8 lanes of the group: afterwards lane j holds
                     // the max over heads of round rj = 2*bit2(j) + bit1(j), i.e. token 4*rj + g
                     uint32_t key[4];
@@ -533,37 +584,93 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
 
                 // ---- 3. online softmax + P.V on tensor cores ------------------------------
                 if (a.attend) {
-                    float z[4];
-                    float mx = -INFINITY;
+                    bool any_raise = false;
+                    if constexpr (MODE == 0) {
+                        float z[4];
+                        float mx = -INFINITY;
 #pragma unroll
-                    for (int r = 0; r < 4; ++r) {
-                        const int t = 4 * r + g;
-                        z[r] = (t < nv && hl < G) ? sc[r] * a.logit_log2 : -INFINITY;
-                        mx = fmaxf(mx, z[r]);
-                    }
-                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-                    // Lazy rescaling: the running reference max only moves when the tile max
-                    // exceeds it by more than 2^8, so P stays <= 256 (exact range for bf16/fp16
-                    // and fp32 sums) and the accumulator is rescaled only on those rare tiles.
-                    const bool raise = mx > m_run + kRescaleLog2;   // includes m_run == -inf
-                    const bool any_raise = __any_sync(0xffffffffu, raise);
-                    if (any_raise) {
-                        const float m_new = raise ? mx : m_run;
-                        const float alpha = raise ? ex2(m_run - m_new) : 1.0f;   // ex2(-inf) = 0
-                        l_run *= alpha;
-                        m_run = m_new;
-                        if (head_writer && g == 0) sm.alpha[warp][hl] = alpha;
-                    }
-                    const bool live = m_run != -INFINITY;
-                    float psum = 0.0f;
+                        for (int r = 0; r < 4; ++r) {
+                            const int t = 4 * r + g;
+                            z[r] = (t < nv && hl < G) ? sc[r] * a.logit_log2 : -INFINITY;
+                            mx = fmaxf(mx, z[r]);
+                        }
+                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                        // Lazy rescaling: the running reference max only moves when the tile
+                        // max exceeds it by more than 2^8, so P stays <= 256 (exact range for
+                        // bf16/fp16 and fp32 sums) and the accumulator is rescaled only on
+                        // those rare tiles.
+                        const bool raise = mx > m_run + kRescaleLog2;   // includes m_run == -inf
+                        any_raise = __any_sync(0xffffffffu, raise);
+                        if (any_raise) {
+                            const float m_new = raise ? mx : m_run;
+                            const float alpha = raise ? ex2(m_run - m_new) : 1.0f;   // ex2(-inf) = 0
+                            l_run *= alpha;
+                            m_run = m_new;
+                            if (head_writer && g == 0) sm.alpha[warp][hl] = alpha;
+                        }
+                        const bool live = m_run != -INFINITY;
+                        float psum = 0.0f;
 #pragma unroll
-                    for (int r = 0; r < 4; ++r) {
-                        const float p = live ? ex2(z[r] - m_run) : 0.0f;
-                        psum += p;
-                        if (head_writer) sm.ps[warp][hl][4 * r + g] = to_bits<T>(p);
+                        for (int r = 0; r < 4; ++r) {
+                            const float p = live ? ex2(z[r] - m_run) : 0.0f;
+                            psum += p;
+                            if (head_writer) sm.ps[warp][hl][4 * r + g] = to_bits<T>(p);
+                        }
+                        l_run += psum;
+                    } else {
+                        // logits S[16 tokens x 8 heads] = K tile . q2^T on tensor cores; A
+                        // fragments straight from the swizzled K stage by ldmatrix.  Lane
+                        // holds tokens tA = lane/4 and tA + 8 of heads nA = 2(lane%4), nA + 1
+                        // -- the accumulator's own columns, so rescaling stays in the lane.
+                        float c4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                        const int mi = lane >> 3;
+                        const int tk = (lane & 7) + 8 * (mi & 1);
+#pragma unroll
+                        for (int kk = 0; kk < D / 16; ++kk) {
+                            const int c8 = (kk & 3) * 2 + (mi >> 1);
+                            uint32_t a0, a1, a2, a3;
+                            ldsm_x4(kb + (kk >> 2) * a.half_bytes + tk * 128 + ((c8 ^ (tk & 7)) << 4),
+                                    a0, a1, a2, a3);
+                            mma_16816<kBf16>(c4, a0, a1, a2, a3, qf[kk][0], qf[kk][1]);
+                        }
+                        const int tA = lane >> 2, tB = tA + 8;
+                        const int nA = 2 * (lane & 3), nB = nA + 1;
+                        const float zA0 = (tA < nv && nA < G) ? c4[0] * a.attn_log2 : -INFINITY;
+                        const float zB0 = (tA < nv && nB < G) ? c4[1] * a.attn_log2 : -INFINITY;
+                        const float zA1 = (tB < nv && nA < G) ? c4[2] * a.attn_log2 : -INFINITY;
+                        const float zB1 = (tB < nv && nB < G) ? c4[3] * a.attn_log2 : -INFINITY;
+                        float mxA = fmaxf(zA0, zA1), mxB = fmaxf(zB0, zB1);
+#pragma unroll
+                        for (int o = 4; o < 32; o <<= 1) {
+                            mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, o));
+                            mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, o));
+                        }
+                        const bool raiseA = mxA > mrA + kRescaleLog2;   // includes mr == -inf
+                        const bool raiseB = mxB > mrB + kRescaleLog2;
+                        if (__any_sync(0xffffffffu, raiseA || raiseB)) {
+                            const float alA = raiseA ? ex2(mrA - mxA) : 1.0f;   // ex2(-inf) = 0
+                            const float alB = raiseB ? ex2(mrB - mxB) : 1.0f;
+                            if (raiseA) { lrA *= alA; mrA = mxA; }
+                            if (raiseB) { lrB *= alB; mrB = mxB; }
+#pragma unroll
+                            for (int mt = 0; mt < MT; ++mt) {
+                                acc[mt][0] *= alA; acc[mt][1] *= alB;
+                                acc[mt][2] *= alA; acc[mt][3] *= alB;
+                            }
+                        }
+                        const bool liveA = mrA != -INFINITY, liveB = mrB != -INFINITY;
+                        const float pA0 = liveA ? ex2(zA0 - mrA) : 0.0f;
+                        const float pB0 = liveB ? ex2(zB0 - mrB) : 0.0f;
+                        const float pA1 = liveA ? ex2(zA1 - mrA) : 0.0f;
+                        const float pB1 = liveB ? ex2(zB1 - mrB) : 0.0f;
+                        lrA += pA0 + pA1;
+                        lrB += pB0 + pB1;
+                        sm.ps[warp][nA][tA] = to_bits<T>(pA0);
+                        sm.ps[warp][nB][tA] = to_bits<T>(pB0);
+                        sm.ps[warp][nA][tB] = to_bits<T>(pA1);
+                        sm.ps[warp][nB][tB] = to_bits<T>(pB1);
                     }
-                    l_run += psum;
                     if (nv < kTileTokens) {
                         // zero V rows past the last valid token (their P is 0; keep them finite)
                         for (int i = lane; i < (kTileTokens - nv) * 8 * HALVES; i += 32) {
@@ -576,7 +683,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                     }
                     __syncwarp();
                     const int n0 = 2 * (lane & 3);
-                    if (any_raise) {
+                    if (MODE == 0 && any_raise) {
                         const float al0 = sm.alpha[warp][n0], al1 = sm.alpha[warp][n0 + 1];
 #pragma unroll
                         for (int mt = 0; mt < MT; ++mt) {
@@ -611,15 +718,34 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
         // merge_kernel combines the partials of a sequence once the whole grid is done
         if (a.attend) {
             constexpr int RS = D + 4;
-            float l_tot = l_run + __shfl_xor_sync(0xffffffffu, l_run, 8);
-            l_tot += __shfl_xor_sync(0xffffffffu, l_tot, 16);
             const int64_t cfirst = (b * a.n_tiles) / a.W;
             const int64_t pidx = (c - cfirst) * wph + s;
             float* part = a.partials + ((b * a.maxc * wph + pidx) * a.Hq) * (int64_t)RS;
-            if (head_writer && g == 0 && hl < G) {
-                float* ph = part + (int64_t)(h * G + hl) * RS;
-                ph[D] = m_run;
-                ph[D + 1] = l_tot;
+            if constexpr (MODE == 0) {
+                float l_tot = l_run + __shfl_xor_sync(0xffffffffu, l_run, 8);
+                l_tot += __shfl_xor_sync(0xffffffffu, l_tot, 16);
+                if (head_writer && g == 0 && hl < G) {
+                    float* ph = part + (int64_t)(h * G + hl) * RS;
+                    ph[D] = m_run;
+                    ph[D + 1] = l_tot;
+                }
+            } else {
+#pragma unroll
+                for (int o = 4; o < 32; o <<= 1) {
+                    lrA += __shfl_xor_sync(0xffffffffu, lrA, o);
+                    lrB += __shfl_xor_sync(0xffffffffu, lrB, o);
+                }
+                const int nA = 2 * lane;   // lanes 0..3 write heads 2 lane and 2 lane + 1
+                if (lane < 4 && nA < G) {
+                    float* ph = part + (int64_t)(h * G + nA) * RS;
+                    ph[D] = mrA;
+                    ph[D + 1] = lrA;
+                }
+                if (lane < 4 && nA + 1 < G) {
+                    float* ph = part + (int64_t)(h * G + nA + 1) * RS;
+                    ph[D] = mrB;
+                    ph[D + 1] = lrB;
+                }
             }
             const int n0 = 2 * (lane & 3);
 #pragma unroll
@@ -804,7 +930,7 @@ static bool encode_map(CUtensorMap* map, const void* base, CUtensorMapDataType d
     return r == CUDA_SUCCESS;
 }
 
-template <typename T, int D, int GP>
+template <typename T, int D, int GP, int MODE>
 static cudaError_t launch_t(const FusedParams& f, const Plan& pl, CUtensorMapDataType dt,
                             cudaStream_t stream) {
     CUtensorMap mk, mv;
@@ -819,7 +945,7 @@ static cudaError_t launch_t(const FusedParams& f, const Plan& pl, CUtensorMapDat
     } else {
         mv = mk;
     }
-    auto kern = decode_kernel<T, D, GP>;
+    auto kern = decode_kernel<T, D, GP, MODE>;
     static std::once_flag once;
     static cudaError_t attr_err = cudaSuccess;
     std::call_once(once, [&] {
@@ -850,6 +976,12 @@ static cudaError_t launch_t(const FusedParams& f, const Plan& pl, CUtensorMapDat
     a.kpool = const_cast<void*>(f.k); a.vpool = const_cast<void*>(f.v);
     a.stride_b = f.stride_b; a.stride_h = f.stride_h; a.stride_p = f.stride_p;
     a.stride_t = f.stride_t;
+    const bool two_q = f.q2 != nullptr;
+    a.q2 = two_q ? f.q2 : f.q;
+    a.q2_stride_b = two_q ? f.q2_stride_b : f.q_stride_b;
+    a.q2_stride_h = two_q ? f.q2_stride_h : f.q_stride_h;
+    a.attn_log2 = f.scale_r * f.logit_mul * 1.4426950408889634f;
+    a.score_n = f.has_score_n ? f.score_n : f.N;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -904,24 +1036,26 @@ cudaError_t launch_fused(const FusedParams& p, cudaStream_t st) {
     const int G = p.Hq / p.Hkv;
     const Plan pl = make_plan(p.B, p.N, p.Hkv, p.D, p.attend != 0);
     if (pl.grid == 0) return cudaSuccess;
+    // attention only: tensor-core logits; two queries: canonical scores of q + tensor-core
+    // logits of q2; otherwise one query serves both (canonical scores)
+    const int mode = !p.sal ? 1 : (p.q2 && p.attend) ? 2 : 0;
+    if (mode == 1 && !p.attend) return cudaErrorInvalidValue;
+    const bool bf = p.dtype == RKV_BF16;
+    const auto dt = bf ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const int gp = G <= 2 ? 2 : G <= 4 ? 4 : 8;
+    // MODE 1 has no canonical dots: its group width does not matter, one instance per shape
+#define RKV_LAUNCH(T_, D_)                                                                     \
+    (mode == 1   ? launch_t<T_, D_, 2, 1>(p, pl, dt, st)                                      \
+     : mode == 2 ? (gp == 2 ? launch_t<T_, D_, 2, 2>(p, pl, dt, st)                           \
+                    : gp == 4 ? launch_t<T_, D_, 4, 2>(p, pl, dt, st)                         \
+                              : launch_t<T_, D_, 8, 2>(p, pl, dt, st))                        \
+                 : (gp == 2 ? launch_t<T_, D_, 2, 0>(p, pl, dt, st)                           \
+                    : gp == 4 ? launch_t<T_, D_, 4, 0>(p, pl, dt, st)                         \
+                              : launch_t<T_, D_, 8, 0>(p, pl, dt, st)))
     cudaError_t e;
-    if (p.dtype == RKV_BF16) {
-        const auto dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-        if (p.D == 128) e = G <= 2 ? launch_t<__nv_bfloat16, 128, 2>(p, pl, dt, st)
-                          : G <= 4 ? launch_t<__nv_bfloat16, 128, 4>(p, pl, dt, st)
-                                   : launch_t<__nv_bfloat16, 128, 8>(p, pl, dt, st);
-        else e = G <= 2 ? launch_t<__nv_bfloat16, 64, 2>(p, pl, dt, st)
-               : G <= 4 ? launch_t<__nv_bfloat16, 64, 4>(p, pl, dt, st)
-                        : launch_t<__nv_bfloat16, 64, 8>(p, pl, dt, st);
-    } else {
-        const auto dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-        if (p.D == 128) e = G <= 2 ? launch_t<__half, 128, 2>(p, pl, dt, st)
-                          : G <= 4 ? launch_t<__half, 128, 4>(p, pl, dt, st)
-                                   : launch_t<__half, 128, 8>(p, pl, dt, st);
-        else e = G <= 2 ? launch_t<__half, 64, 2>(p, pl, dt, st)
-               : G <= 4 ? launch_t<__half, 64, 4>(p, pl, dt, st)
-                        : launch_t<__half, 64, 8>(p, pl, dt, st);
-    }
+    if (bf) e = p.D == 128 ? RKV_LAUNCH(__nv_bfloat16, 128) : RKV_LAUNCH(__nv_bfloat16, 64);
+    else e = p.D == 128 ? RKV_LAUNCH(__half, 128) : RKV_LAUNCH(__half, 64);
+#undef RKV_LAUNCH
     return e;
 }
 

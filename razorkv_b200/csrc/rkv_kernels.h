@@ -85,6 +85,10 @@ struct FusedParams {
     // fused append of one new token at position N - 1 (k_new == nullptr: no append)
     const void* k_new; const void* v_new; int64_t new_stride_b, new_stride_h;
     int64_t* pt_w; const int64_t* free_stack; int64_t free_top; int sal_init_norm;
+    // a second (attention) query: q scores, q2 attends (q2 == nullptr: q does both)
+    const void* q2; int64_t q2_stride_b, q2_stride_h;
+    // tokens at or past score_n keep their salience (has_score_n == 0: all are scored)
+    int has_score_n; int64_t score_n;
 };
 
 cudaError_t launch_score(const ScoreParams& p, cudaStream_t st);

@@ -130,3 +130,60 @@ def test_fused_repeated_launches_are_stable():
         assert st == 0
         outs.append(out)
     assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("B,Hq,Hkv,D,N", SHAPES)
+def test_attention_only_matches_oracle(B, Hq, Hkv, D, N, dtype):
+    """rkv_decode_attention on the fast path: logits on tensor cores, no scoring."""
+    kpool, vpool, spool, pt, q = _setup(B, Hq, Hkv, D, N, dtype, seed=B * 17 + N)
+    kd, vd, ptd, qd = (t.cuda() for t in (kpool, vpool, pt, q))
+    out = torch.empty_like(qd)
+    lib = _lib.load()
+    lay = _layout(kd, vd, ptd, N)
+    qs = Query(qd.data_ptr(), dtype_code(dtype), Hq, 1, qd.stride(0), qd.stride(1), qd.stride(2))
+    os_ = Output(out.data_ptr(), dtype_code(dtype), 0, out.stride(0), out.stride(1), out.stride(2))
+    ws = Workspace.get(qd.device, lib.rkv_decode_attention_workspace_size(qs, lay))
+    assert lib.rkv_decode_attention(qs, lay, 0.0, 0, os_, ws.data_ptr(), ws.numel(),
+                                    torch.cuda.current_stream().cuda_stream) == 0
+    torch.cuda.synchronize()
+    assert int(ws[:4].view(torch.int32)[0]) == 0
+    ref = O.attention(q.float().numpy(), _logical(kpool, pt, N).float().numpy(),
+                      _logical(vpool, pt, N).float().numpy())
+    np.testing.assert_allclose(out.float().cpu().numpy(), ref, atol=2e-2, rtol=1e-2)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("B,Hq,Hkv,D,N", SHAPES)
+def test_scored_matches_oracle(B, Hq, Hkv, D, N, dtype):
+    """rkv_decode_scored (the HF hook step): the salience of the tokens before score_tokens
+    takes the EWMA of q_score's resonance bit for bit, later tokens keep theirs, and the
+    output is q_attn's attention over every token."""
+    kpool, vpool, spool, pt, q = _setup(B, Hq, Hkv, D, N, dtype, seed=B * 29 + N)
+    q_attn = torch.randn(B, Hq, 1, D, generator=torch.Generator().manual_seed(N)).to(dtype)
+    score_tokens = max(0, N - 1 - N % 3)
+    kd, vd, sd, ptd, qd, qad = (t.cuda() for t in (kpool, vpool, spool, pt, q, q_attn))
+    out = torch.empty_like(qd)
+    lib = _lib.load()
+    lay = _layout(kd, vd, ptd, N)
+    mk = lambda t: Query(t.data_ptr(), dtype_code(dtype), Hq, 1, t.stride(0), t.stride(1), t.stride(2))
+    qs, qas = mk(qd), mk(qad)
+    os_ = Output(out.data_ptr(), dtype_code(dtype), 0, out.stride(0), out.stride(1), out.stride(2))
+    sal = Salience(sd.data_ptr(), sd.stride(1), sd.stride(0))
+    ws = Workspace.get(qd.device, lib.rkv_decode_scored_workspace_size(qas, lay))
+    assert lib.rkv_decode_scored(qs, qas, lay, sal, score_tokens, 0.98, 1.0 - 0.98, 0.0, os_,
+                                 ws.data_ptr(), ws.numel(),
+                                 torch.cuda.current_stream().cuda_stream) == 0
+    torch.cuda.synchronize()
+    assert int(ws[:4].view(torch.int32)[0]) == 0
+    K = _logical(kpool, pt, N).float().numpy()
+    V = _logical(vpool, pt, N).float().numpy()
+    S0 = _sal_logical(spool, pt, N).numpy()
+    expect_S = S0.copy()
+    if score_tokens:
+        R = O.resonance(q.float().numpy(), K[:, :, :score_tokens], 2)
+        expect_S[:, :score_tokens] = O.ewma(S0[:, :score_tokens], R, 0.98)
+    got_S = _sal_logical(sd.cpu(), pt, N).numpy()
+    assert np.array_equal(got_S.view(np.uint32), expect_S.view(np.uint32))
+    ref = O.attention(q_attn.float().numpy(), K, V)
+    np.testing.assert_allclose(out.float().cpu().numpy(), ref, atol=2e-2, rtol=1e-2)
