@@ -59,6 +59,8 @@ SHAPES = [
     (5, 40, 8, 128, 3),        # fewer tokens than a page
     (2, 6, 2, 128, 900),       # G = 3: the second query-head slice has one live head
     (3, 16, 8, 128, 1500),     # G = 2
+    (2, 16, 2, 64, 700),       # G = 8 over 2 kv heads: query heads split over two warps
+    (3, 6, 1, 128, 333),       # G = 6, 1 kv head: split, second warp with 2 live heads
 ]
 
 
