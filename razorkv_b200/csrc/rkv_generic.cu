@@ -279,14 +279,51 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_sums, int* 
     return res;
 }
 
+constexpr int kSelSmemKeys = 11264;   // keys kept in shared memory up to this many pages (44 KiB)
+
+// Warp 0 picks the radix digit holding the rem-th largest key: lane l owns bins 8l..8l+7,
+// a suffix scan over lanes (highest digits first) finds the owning lane, which walks its 8
+// bins.  Writes the digit and the count still to take among keys with that digit.
+__device__ __forceinline__ void select_digit(const int* hist, int rem, uint32_t prefix, int shift,
+                                             uint32_t* s_prefix, int* s_remaining) {
+    const int lane = threadIdx.x & 31;
+    int c[8];
+    int mine = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) { c[i] = hist[8 * lane + i]; mine += c[i]; }
+    // inclusive sum over lanes >= lane (digits from the top)
+    int above = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_down_sync(0xffffffffu, above, o);
+        if (lane + o < 32) above += y;
+    }
+    const int before = above - mine;   // keys in higher lanes' bins
+    const bool here = before < rem && above >= rem;
+    if (here) {
+        int cum = before;
+#pragma unroll
+        for (int i = 7; i >= 0; --i) {
+            if (cum + c[i] >= rem) {
+                *s_prefix = prefix | ((uint32_t)(8 * lane + i) << shift);
+                *s_remaining = rem - cum;
+                break;
+            }
+            cum += c[i];
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kSelThreads)
 select_kernel(const float* scores, int64_t B, int64_t n, int64_t k, int64_t* kept, float* margin,
-              uint32_t* keys) {
+              uint32_t* gkeys) {
     __shared__ int hist[256];
     __shared__ int warp_sums[32];
     __shared__ uint32_t s_prefix;
     __shared__ int s_remaining;
     __shared__ uint32_t s_best_out;
+    __shared__ uint32_t s_keys[kSelSmemKeys];
+    uint32_t* keys = n <= kSelSmemKeys ? s_keys : gkeys;   // uniform over the CTA
     for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
         float acc = scores[i];
         if (B > 1) {
@@ -302,22 +339,13 @@ select_kernel(const float* scores, int64_t B, int64_t n, int64_t k, int64_t* kep
         for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
         __syncthreads();
         const uint32_t prefix = s_prefix;
+        const int rem = s_remaining;
         for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
             uint32_t key = keys[i];
             if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1);
         }
         __syncthreads();
-        if (threadIdx.x == 0) {
-            int cum = 0, rem = s_remaining;
-            for (int d = 255; d >= 0; --d) {
-                if (cum + hist[d] >= rem) {
-                    s_prefix = prefix | ((uint32_t)d << shift);
-                    s_remaining = rem - cum;
-                    break;
-                }
-                cum += hist[d];
-            }
-        }
+        if (threadIdx.x < 32) select_digit(hist, rem, prefix, shift, &s_prefix, &s_remaining);
         mask |= 255u << shift;
         __syncthreads();
     }

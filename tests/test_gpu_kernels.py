@@ -130,7 +130,9 @@ def test_score_bit_exact(dtype, D, Hq, Hkv, QL):
 
 
 @pytest.mark.parametrize("B,n,k", [(1, 222, 66), (8, 1400, 700), (2, 5, 5), (3, 8192, 1000),
-                                   (1, 1, 1), (4, 3000, 1)])
+                                   (1, 1, 1), (4, 3000, 1),
+                                   # keys in shared memory up to 11264 pages, global above
+                                   (1, 11264, 5000), (2, 11265, 3), (2, 20000, 7000)])
 def test_select_pages_exact(B, n, k):
     g = torch.Generator().manual_seed(n + k)
     scores = (torch.randn(B, n, generator=g) * 2 + 10).float()
