@@ -124,6 +124,14 @@ unsigned long long rkv_launch_count(void);
  * flag the decode kernels set when a bounded wait gives up (0 = no error). */
 size_t rkv_workspace_error_flag_offset(void);
 
+/* Self-test of the bounded waits (no reference counterpart).  One CTA waits on a barrier
+ * that nothing arrives on, with a limit of limit_cycles SM cycles (1 .. 1e10): the wait gives
+ * up and sets result[0] to 1, as the decode kernels set the workspace error flag; result[1]
+ * is 1 if any wait reported success (expected 0); result[2] is 1 if a second wait after the
+ * abort returned at once (expected 1).  result: 3 device int32 zeroed by the caller.  The
+ * kernel ends normally and the context stays usable. */
+int rkv_selftest_wait_timeout(int* result, long long limit_cycles, void* stream);
+
 /* ---- attention --------------------------------------------------------------------------
  * out = softmax(q.k * scale) . v over the num_tokens tokens of each (b, kv-head), GQA head
  * h reading kv head h / (Hq/Hkv).  causal != 0 masks key t > query row (upper-left aligned).

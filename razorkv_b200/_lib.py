@@ -61,6 +61,7 @@ _SIGNATURES = {
     "rkv_abi_version": (ctypes.c_int, []),
     "rkv_launch_count": (ctypes.c_ulonglong, []),
     "rkv_workspace_error_flag_offset": (c_sz, []),
+    "rkv_selftest_wait_timeout": (ctypes.c_int, [c_vp, ctypes.c_longlong, c_vp]),
     "rkv_decode_attention_workspace_size": (c_sz, [P(Query), P(KVLayout)]),
     "rkv_decode_attention": (ctypes.c_int, [P(Query), P(KVLayout), c_f32, ctypes.c_int,
                                             P(Output), c_vp, c_sz, c_vp]),

@@ -125,6 +125,11 @@ int rkv_abi_version(void) { return 1; }
 
 unsigned long long rkv_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
+int rkv_selftest_wait_timeout(int* result, long long limit_cycles, void* stream) {
+    if (!result || limit_cycles < 1 || limit_cycles > 10000000000LL) return RKV_ERR_INVALID_ARGUMENT;
+    return status_of(launch_wait_selftest(result, limit_cycles, S(stream)));
+}
+
 size_t rkv_decode_attention_workspace_size(const rkv_query* q, const rkv_kv_layout* kv) {
     if (!q || !kv) return 0;
     const int64_t G = q->num_heads / (kv->num_kv_heads > 0 ? kv->num_kv_heads : 1);

@@ -857,6 +857,28 @@ static int num_sms() {
     return cached[dev];
 }
 
+// Self-test of the bounded waits: every thread of one CTA waits on a barrier that nothing
+// arrives on.  The first to reach the limit sets the CTA abort flag and the error flag; the
+// others then return at once.  result[1]: some wait reported success (expected 0);
+// result[2]: a second wait after the abort returned within half the limit (expected 1).
+__global__ void __launch_bounds__(64) wait_timeout_kernel(int* result, long long limit) {
+    __shared__ uint64_t bar;
+    __shared__ int abort;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    const bool first = mbar_wait(&bar, 0, result, &abort, limit);
+    const long long t0 = clock64();
+    const bool second = mbar_wait(&bar, 0, result, &abort, limit);
+    const bool quick = clock64() - t0 < limit / 2;
+    if (first || second) atomicExch(result + 1, 1);
+    __syncthreads();
+    if (threadIdx.x == 0) result[2] = quick ? 1 : 0;
+}
+
 struct Plan {
     int64_t n_tiles, total, W, grid, maxc;
     int wph, stages, stage_bytes, tile_bytes, kv_tile_bytes, half_bytes, smem_bytes;
@@ -1027,6 +1049,11 @@ size_t fused_workspace_bytes(int64_t B, int Hq, int Hkv, int D, int64_t N) {
     if (B <= 0 || Hkv <= 0) return 0;
     sm100::Plan pl = sm100::make_plan(B, N, Hkv, D, true);
     return (size_t)B * pl.maxc * pl.wph * Hq * (D + 4) * sizeof(float);
+}
+
+cudaError_t launch_wait_selftest(int* result, long long limit, cudaStream_t st) {
+    sm100::wait_timeout_kernel<<<1, 64, 0, st>>>(result, limit);
+    return counted(cudaGetLastError(), 1);
 }
 
 cudaError_t launch_fused(const FusedParams& p, cudaStream_t st) {

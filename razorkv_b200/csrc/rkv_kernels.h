@@ -116,5 +116,6 @@ bool fused_supported(int dtype, int D, int Hkv, int Hq, int64_t page_size, int64
                      const void* v);
 size_t fused_workspace_bytes(int64_t B, int Hq, int Hkv, int D, int64_t N);
 cudaError_t launch_fused(const FusedParams& p, cudaStream_t st);
+cudaError_t launch_wait_selftest(int* result, long long limit, cudaStream_t st);
 
 }  // namespace rkv

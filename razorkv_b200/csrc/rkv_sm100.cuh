@@ -56,13 +56,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // wait of the CTA returns false at once, so all warps run their loops to the end without
 // waiting (and without skipping any named barrier) and the kernel finishes.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err,
-                                          volatile int* abort) {
+                                          volatile int* abort,
+                                          long long limit = kWaitLimitCycles) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long start = clock64();
     while (true) {
         if (*abort) return false;
         if (mbar_try_wait(bar, parity)) return true;
-        if (clock64() - start > kWaitLimitCycles) {
+        if (clock64() - start > limit) {
             *abort = 1;
             if (err) atomicExch(err, 1);
             return false;
