@@ -968,13 +968,21 @@ static cudaError_t launch_t(const FusedParams& f, const Plan& pl, CUtensorMapDat
         mv = mk;
     }
     auto kern = decode_kernel<T, D, GP, MODE>;
-    static std::once_flag once;
-    static cudaError_t attr_err = cudaSuccess;
-    std::call_once(once, [&] {
-        attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        kSmemBudget + (int)sizeof(SmemTail) + 1024);
-    });
-    if (attr_err != cudaSuccess) return attr_err;
+    {
+        // function attributes are per device: set once on each device this process uses
+        static std::mutex mu;
+        static bool done[64] = {false};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        std::lock_guard<std::mutex> lock(mu);
+        if (dev < 0 || dev >= 64 || !done[dev]) {
+            const cudaError_t e = cudaFuncSetAttribute(
+                kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                kSmemBudget + (int)sizeof(SmemTail) + 1024);
+            if (e != cudaSuccess) return e;
+            if (dev >= 0 && dev < 64) done[dev] = true;
+        }
+    }
     DevArgs a{};
     a.q = f.q; a.q_stride_b = f.q_stride_b; a.q_stride_h = f.q_stride_h;
     a.Hq = f.Hq; a.Hkv = f.Hkv; a.G = f.Hq / f.Hkv; a.wph = pl.wph;

@@ -61,6 +61,10 @@ SHAPES = [
     (3, 16, 8, 128, 1500),     # G = 2
     (2, 16, 2, 64, 700),       # G = 8 over 2 kv heads: query heads split over two warps
     (3, 6, 1, 128, 333),       # G = 6, 1 kv head: split, second warp with 2 live heads
+    # a CTA on every SM, CTA ranges crossing sequence boundaries, tens of partials a row
+    (4, 32, 8, 128, 2000),     # ~37 partials a row
+    (8, 16, 4, 64, 4000),      # head_dim 64, 2 tiles per stage
+    (16, 8, 8, 128, 700),      # G = 1, 16 sequences
 ]
 
 
