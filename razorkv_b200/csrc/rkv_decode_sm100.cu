@@ -32,6 +32,7 @@
 // the last page are masked and their V rows zeroed.
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cooperative_groups.h>
 #include <cuda_fp16.h>
 #include <math.h>
 
@@ -763,17 +764,25 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
     }
 }
 
-// Log-sum-exp merge of the per-warp partials: one CTA per (sequence, query head) of
-// kMergeGroups x D threads.  Group g folds its share of the partials with one lane per
-// output dimension (every partial's (m, l, acc[d]) of a 32-partial chunk is loaded at once;
-// the weights 2^(m_p - M) go through shuffles); the groups then combine in shared memory.
-// Splitting the partials over groups bounds the chain of dependent L2 round trips when one
-// sequence has hundreds of partials (batch 1).
+// Log-sum-exp merge of the per-warp partials of each (sequence b, query head hq) row.
+// merge_kernel: one CTA per row of kMergeGroups x D threads.  Group g folds its share of the
+// partials with one lane per output dimension (every partial's (m, l, acc[d]) of a 32-partial
+// chunk is loaded at once; the weights 2^(m_p - M) go through shuffles); the groups then
+// combine in shared memory.
+// merge_cluster_kernel, for rows with more than kMergePartialsPerCta partials (batch 1: a row
+// has 150-300): a cluster of S <= kMergeMaxCluster CTAs serves one row, CTA r folding the
+// contiguous share [np r / S, np (r + 1) / S) as above, then storing its fold into slot r of
+// cluster rank 0's shared memory (distributed shared memory); after one cluster barrier rank
+// 0 folds the S results in rank order and writes the row.  With one CTA per row a batch-1
+// launch merged its 28-32 rows on 28-32 SMs.
 constexpr int kMergeGroups = 4;
+constexpr int kMergeMaxCluster = 8;
+constexpr int kMergePartialsPerCta = 40;   // cluster size: ceil(partials / 40), at most 8
 
 struct MergeArgs {
     const float* partials; void* out; int64_t o_stride_b, o_stride_h;
     int Hq, wph; int64_t n_tiles, W, maxc;
+    int cluster;   // CTAs per row (the launch's cluster size)
 };
 
 template <typename T, int D>
@@ -841,6 +850,117 @@ merge_kernel(const MergeArgs a) {
     }
     T* ob = static_cast<T*>(a.out) + b * a.o_stride_b + (int64_t)hq * a.o_stride_h;
     ob[d] = from_f<T>(Lt > 0.f ? Ot / Lt : 0.f);
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kMergeGroups * D)
+merge_cluster_kernel(const MergeArgs a) {
+    // the next decode kernel may start its prologue now; it waits for this grid to finish
+    // before it touches anything this grid reads
+    grid_launch_dependents();
+    grid_dependency_wait();   // the partials come from the decode kernel just before
+    constexpr int RS = D + 4;
+    __shared__ float s_o[kMergeGroups][D];
+    __shared__ float s_m[kMergeGroups], s_l[kMergeGroups];
+    // rank 0 of a cluster: the folds of the cluster's CTAs, slot r from rank r
+    __shared__ float c_o[kMergeMaxCluster][D];
+    __shared__ float c_m[kMergeMaxCluster], c_l[kMergeMaxCluster];
+    const int lane = threadIdx.x & 31;
+    const int grp = threadIdx.x / D;
+    const int d = threadIdx.x % D;
+    const int S = a.cluster;
+    const int rank = (int)(blockIdx.x % (unsigned)S);   // == the block's rank in its cluster
+    const int row = (int)(blockIdx.x / (unsigned)S);
+    const int64_t b = row / a.Hq;
+    const int hq = row % a.Hq;
+    const int64_t cfirst = (b * a.n_tiles) / a.W;
+    const int64_t clast = ((b + 1) * a.n_tiles - 1) / a.W;
+    const int np = (int)(clast - cfirst + 1) * a.wph;
+    // this CTA's share of the row; group g takes its 32-partial chunks g, g + G, ...
+    const int lo = np * rank / S, hi = np * (rank + 1) / S;
+    const float* pb = a.partials + ((b * a.maxc * a.wph) * a.Hq + hq) * (int64_t)RS;
+    const int64_t pstride = (int64_t)a.Hq * RS;
+    float M = -INFINITY, O = 0.f, L = 0.f;
+    for (int p0 = lo + grp * 32; p0 < hi; p0 += kMergeGroups * 32) {
+        const int n = min(32, hi - p0);
+        // lane p holds the stats of partial p0 + p
+        const float mp = lane < n ? __ldcg(pb + (p0 + lane) * pstride + D) : -INFINITY;
+        const float lp = lane < n ? __ldcg(pb + (p0 + lane) * pstride + D + 1) : 0.f;
+        float acc[32];
+        const float* pp = pb + p0 * pstride + d;   // walks the chunk's partials
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            acc[i] = i < n ? __ldcg(pp) : 0.f;
+            pp += pstride;
+        }
+        float Mc = mp;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) Mc = fmaxf(Mc, __shfl_xor_sync(0xffffffffu, Mc, o));
+        const float Mn = fmaxf(M, Mc);
+        if (Mn == -INFINITY) continue;
+        const float r = M == -INFINITY ? 0.f : ex2(M - Mn);
+        const float wl = mp == -INFINITY ? 0.f : ex2(mp - Mn);
+        float Lc = lp * wl;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) Lc += __shfl_xor_sync(0xffffffffu, Lc, o);
+        float Oc = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) Oc += acc[i] * __shfl_sync(0xffffffffu, wl, i);
+        O = O * r + Oc;
+        L = L * r + Lc;
+        M = Mn;
+    }
+    s_o[grp][d] = O;
+    if (d == 0) { s_m[grp] = M; s_l[grp] = L; }
+    __syncthreads();
+    if (grp == 0) {
+        float Mt = -INFINITY;
+#pragma unroll
+        for (int g = 0; g < kMergeGroups; ++g) Mt = fmaxf(Mt, s_m[g]);
+        float Ot = 0.f, Lt = 0.f;
+        if (Mt != -INFINITY) {
+#pragma unroll
+            for (int g = 0; g < kMergeGroups; ++g) {
+                const float w = s_m[g] == -INFINITY ? 0.f : ex2(s_m[g] - Mt);
+                Ot += s_o[g][d] * w;
+                Lt += s_l[g] * w;
+            }
+        }
+        // push this CTA's fold into cluster rank 0's slot `rank` (distributed shared memory
+        // stores; the cluster barrier below releases them)
+        namespace cg = cooperative_groups;
+        cg::cluster_group cluster = cg::this_cluster();
+        *cluster.map_shared_rank(&c_o[rank][d], 0) = Ot;
+        if (d == 0) {
+            *cluster.map_shared_rank(&c_m[rank], 0) = Mt;
+            *cluster.map_shared_rank(&c_l[rank], 0) = Lt;
+        }
+    }
+    {
+        // every thread of every CTA of the cluster reaches the barrier (no early return);
+        // after it only rank 0 reads, and only its own shared memory
+        namespace cg = cooperative_groups;
+        cg::this_cluster().sync();
+        if (rank == 0 && grp == 0) {
+            float Mt = -INFINITY;
+#pragma unroll
+            for (int r = 0; r < kMergeMaxCluster; ++r)
+                if (r < S) Mt = fmaxf(Mt, c_m[r]);
+            float Ot = 0.f, Lt = 0.f;
+            if (Mt != -INFINITY) {
+#pragma unroll
+                for (int r = 0; r < kMergeMaxCluster; ++r) {
+                    if (r < S) {
+                        const float w = c_m[r] == -INFINITY ? 0.f : ex2(c_m[r] - Mt);
+                        Ot += c_o[r][d] * w;
+                        Lt += c_l[r] * w;
+                    }
+                }
+            }
+            T* ob = static_cast<T*>(a.out) + b * a.o_stride_b + (int64_t)hq * a.o_stride_h;
+            ob[d] = from_f<T>(Lt > 0.f ? Ot / Lt : 0.f);
+        }
+    }
 }
 
 // ------------------------------------------------------------------------------ host side
@@ -1024,14 +1144,26 @@ static cudaError_t launch_t(const FusedParams& f, const Plan& pl, CUtensorMapDat
     cfg.numAttrs = 1;
     cudaError_t e = counted(cudaLaunchKernelEx(&cfg, kern, mk, mv, a), 1);
     if (e != cudaSuccess || !f.attend) return e;
+    // CTAs per row: enough that each folds ~kMergePartialsPerCta partials (rows of a batch-1
+    // launch have hundreds); maxc * wph bounds the partials of every row
+    const int64_t np_max = pl.maxc * pl.wph;
+    int S = (int)((np_max + kMergePartialsPerCta - 1) / kMergePartialsPerCta);
+    S = S < 1 ? 1 : S > kMergeMaxCluster ? kMergeMaxCluster : S;
     MergeArgs m{f.partials, f.out, f.o_stride_b, f.o_stride_h, f.Hq, pl.wph, pl.n_tiles, pl.W,
-                pl.maxc};
+                pl.maxc, S};
+    cudaLaunchAttribute mattr[2];
+    mattr[0] = attr[0];
+    mattr[1].id = cudaLaunchAttributeClusterDimension;
+    mattr[1].val.clusterDim.x = (unsigned)S;
+    mattr[1].val.clusterDim.y = 1;
+    mattr[1].val.clusterDim.z = 1;
     cudaLaunchConfig_t mcfg{};
-    mcfg.gridDim = dim3((unsigned)(f.B * f.Hq));
+    mcfg.gridDim = dim3((unsigned)(f.B * f.Hq * S));
     mcfg.blockDim = dim3(kMergeGroups * D);
     mcfg.stream = stream;
-    mcfg.attrs = attr;
-    mcfg.numAttrs = 1;
+    mcfg.attrs = mattr;
+    mcfg.numAttrs = S > 1 ? 2 : 1;
+    if (S > 1) return counted(cudaLaunchKernelEx(&mcfg, merge_cluster_kernel<T, D>, m), 1);
     return counted(cudaLaunchKernelEx(&mcfg, merge_kernel<T, D>, m), 1);
 }
 
