@@ -65,6 +65,9 @@ SHAPES = [
     (4, 32, 8, 128, 2000),     # ~37 partials a row
     (8, 16, 4, 64, 4000),      # head_dim 64, 2 tiles per stage
     (16, 8, 8, 128, 700),      # G = 1, 16 sequences
+    # batch 1, hundreds of partials a row: the merge spreads each row over a CTA cluster
+    (1, 16, 2, 64, 20000),     # ~560 partials a row: clusters of 8
+    (1, 28, 4, 128, 20000),    # ~280 partials a row: clusters of 7
 ]
 
 
