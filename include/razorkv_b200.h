@@ -115,8 +115,8 @@ int rkv_abi_version(void);
 unsigned long long rkv_launch_count(void);
 
 /* Every workspace passed to this library must start with RKV_WORKSPACE_HEADER_BYTES of
- * zeros before its first use.  The decode kernels keep their cross-CTA merge counters and
- * an error flag there and leave the counters at zero when each launch completes; all other
+ * zeros before its first use.  The decode kernels keep an error flag there; the rest of the
+ * header is reserved for cross-CTA counters, which every launch leaves at zero.  All other
  * workspace use starts after the header.  The *_workspace_size queries include the header. */
 #define RKV_WORKSPACE_HEADER_BYTES 65536
 

@@ -241,9 +241,12 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
     const int Hkv = a.Hkv;
 
     // Before the wait on the previous kernel: fetch the tensor maps and warm L2 with the
-    // pages of the first stages.  Page ids read here may be stale (the previous kernel may
+    // pages of the first stage.  Page ids read here may be stale (the previous kernel may
     // still rewrite the table), which only makes a prefetch useless; they bypass L1, and
-    // every load that feeds the computation happens after the wait.
+    // every load that feeds the computation happens after the wait.  Only the first stage:
+    // prefetching all NS stages (28 MB over the grid) kept DRAM busy through the wait
+    // release, and the page-table and q loads that gate the first TMA queued behind it
+    // (first tile ~1 us later per launch).
     if (warp == kComputeWarps && lane == 0) {
         prefetch_tensormap(&tmk);
         if (a.attend) prefetch_tensormap(&tmv);
@@ -251,7 +254,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
             const int64_t b = r0 / a.n_tiles;
             const int64_t t_begin = r0 - b * a.n_tiles;
             const int64_t t_seg = min(r1, (b + 1) * a.n_tiles) - b * a.n_tiles;
-            const int64_t t_end = min(t_seg, t_begin + (int64_t)NS * wph);
+            const int64_t t_end = min(t_seg, t_begin + (int64_t)wph);
             for (int64_t t = t_begin; t < t_end; ++t) {
                 const int64_t v = __ldcg(a.pt + b * a.pt_stride_b + t);
                 if (v < 0 || v >= a.num_slots) continue;
