@@ -36,6 +36,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -84,11 +85,10 @@ class ClockSampler:
     def __init__(self, gpu_index):
         self.gpu = gpu_index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+        self.path = os.path.join(tempfile.gettempdir(), f"rkv_clocks_{os.getpid()}_{gpu_index}.csv")
 
     def start(self):
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -107,19 +107,24 @@ class ClockSampler:
         self.f.close()
         sm, mx, reasons = [], 0.0, set()
         with open(self.path) as f:
-            for line in f:
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) < 9 or not parts[0].isdigit() or int(parts[0]) != self.gpu:
-                    continue
-                try:
-                    sm.append(float(parts[1]))
-                    mx = max(mx, float(parts[2]))
-                except ValueError:
-                    continue
-                names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-                for n, v in zip(names, parts[5:9]):
-                    if v.lower().startswith("active"):
-                        reasons.add(n)
+            lines = f.readlines()
+        try:
+            os.remove(self.path)
+        except OSError:
+            pass
+        for line in lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9 or not parts[0].isdigit() or int(parts[0]) != self.gpu:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
@@ -198,13 +203,19 @@ def traffic_per_byte():
 
 
 # ---------------------------------------------------------------------------- CPU oracle arm
-def oracle_sample(w, steps, warmup=0, threads=None):
-    """Time the CPU oracle (reference algorithm) on a bounded sample of workload w.
+def oracle_sample(w, steps, warmup=0, threads=None, parity_dev=None):
+    """Time the CPU oracle (reference algorithm) on a bounded sample of workload w and, with
+    ``parity_dev``, run the GPU cache beside it on the same CPU-drawn inputs.
 
     Sample: the shallowest and deepest layers (0 and L-1) at the full batch after a full
-    prefill; every decode step runs update(k, v, l, q) + attention on those two layers.
-    A full step's time is extrapolated by retained tokens: sum over all layers of the
-    layer's retained tokens times the measured seconds per retained token."""
+    prefill (which compacts every layer to its budget); every decode step runs
+    update(k, v, l, q) + attention on those two layers.  A full step's time is extrapolated:
+    the measured seconds per retained token of the sampled layers times the retained tokens
+    of all L layers (the sampled layers' measured counts, the budget for the others).
+
+    Parity (GPU cache vs oracle, same inputs): the kept pages of every compaction decision,
+    the salience of the sampled layers after the last step (bit for bit), the largest
+    absolute difference of the attention outputs, and the smallest top-k margin met."""
     import numpy as np
     import torch
     from oracle import razorkv_oracle as O
@@ -223,11 +234,20 @@ def oracle_sample(w, steps, warmup=0, threads=None):
     layers = sorted({0, L - 1})
     elt = torch.tensor([], dtype=w.dtype).element_size()
     cache = O.OracleCache(ocfg, L, elt)
+    gcache = None
+    if parity_dev is not None:
+        from razorkv_b200 import PagedRazorKVCache
+        gcache = PagedRazorKVCache(cfg, L)
+        gcache.record_decisions = True
     for l in layers:
         K, V, q0 = layer_prefill(w, l, "cpu")
         cache.update(K.float().numpy(), V.float().numpy(), l, q0.float().numpy())
+        if gcache is not None:
+            gcache.update(K.to(parity_dev), V.to(parity_dev), l, {"query_states": q0.to(parity_dev)})
         del K, V
-    tot_time, tot_tokens, step_times = 0.0, 0, []
+    n_prefill_dec = len(cache.decisions)
+    tot_time, tot_tokens = 0.0, 0
+    max_err = 0.0
     for step in range(warmup + steps):
         t_step, n_step = 0.0, 0
         for l in layers:
@@ -235,29 +255,60 @@ def oracle_sample(w, steps, warmup=0, threads=None):
             qn, kn, vn = q.float().numpy(), k.float().numpy(), v.float().numpy()
             t0 = time.perf_counter()
             Kc, Vc = cache.update(kn, vn, l, qn)
-            O.attention(qn, Kc, Vc)
+            ref = O.attention(qn, Kc, Vc)
             t_step += time.perf_counter() - t0
             n_step += Kc.shape[2]
+            if gcache is not None:
+                out = gcache.decode_step(q.to(parity_dev), k.to(parity_dev), v.to(parity_dev), l)
+                max_err = max(max_err, float(np.max(np.abs(out.float().cpu().numpy() - ref))))
         if step >= warmup:
             tot_time += t_step
             tot_tokens += n_step
-            step_times.append(t_step / n_step)
     sec_per_token = tot_time / max(tot_tokens, 1)
-    # retained tokens of every layer at this point of the decode (budget of the final length)
     T = cache.seen
-    retained = sum(ocfg.budget(l, L, T) for l in range(L))
+    retained = sum(cache.K[l].shape[2] if l in layers else ocfg.budget(l, L, T) for l in range(L))
     est_step = sec_per_token * retained
-    return {
+    decode_evictions = len(cache.decisions) - n_prefill_dec
+    res = {
         "value": w.batch / est_step,
         "unit": "tokens/s",
         "cores": cores,
         "kind": "port",
-        "sample": (f"layers {layers} of {L}, batch {w.batch}, {w.context}-token prefill, "
-                   f"{steps} timed decode steps; full-step time extrapolated by retained tokens "
-                   f"({retained} over {L} layers)"),
+        "sample": (f"layers {layers} of {L}, batch {w.batch}, {w.context}-token prefill "
+                   f"(untimed), {steps} timed decode steps with {decode_evictions} decode-time "
+                   f"compactions; the full-step time is EXTRAPOLATED from the sampled layers' "
+                   f"seconds per retained token to {retained} retained tokens over {L} layers"),
         "ms_per_step_est": est_step * 1e3,
         "sampled_seconds": tot_time,
+        "decode_evictions_in_sample": decode_evictions,
     }
+    if gcache is not None:
+        torch.cuda.synchronize(parity_dev)
+        gcache.check_errors()
+        kept_equal = len(gcache.decisions) == len(cache.decisions)
+        margins = []
+        for gd, od in zip(gcache.decisions, cache.decisions):
+            if gd.kind == "pages":
+                kept_equal &= gd.layer == od.layer and np.array_equal(gd.kept.cpu().numpy(), od.kept)
+                margins.append(float(gd.margin.item()))
+            else:
+                kept_equal &= od.kind == "zones"
+        sal_equal = all(
+            np.array_equal(gcache.salience_scores[l].cpu().numpy().view(np.uint32),
+                           cache.S[l].view(np.uint32)) for l in layers)
+        res["parity"] = {
+            "kept_pages_equal": bool(kept_equal),
+            "salience_bitexact": bool(sal_equal),
+            "max_abs_err": max_err,
+            "tolerance": "2e-2 abs / 1e-2 rel (bf16)" if w.dtype == torch.bfloat16 else "1e-5 rel (fp32)",
+            "min_topk_margin": min(margins) if margins else None,
+            "decisions": len(cache.decisions),
+            "against": "oracle (CPU restatement pinned to the reference's decisions on this "
+                       "workload's layers 0 and L-1 by tests/test_oracle_scale.py)",
+            "sample": f"layers {layers}, CPU-drawn inputs, prefill + {warmup + steps} decode steps",
+        }
+        del gcache
+    return res
 
 
 def run_reference(args):
@@ -281,6 +332,7 @@ def run_reference(args):
         "steps": steps,
         "warmup": warm,
         "ms_per_step": res["ms_per_step_est"],
+        "ms_per_step_kind": "extrapolated from the sampled layers (see cpu_baseline.sample)",
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
@@ -477,6 +529,7 @@ def main():
         dist.barrier()
     timer.enabled = True
     launches0 = lib.rkv_launch_count()
+    compactions0 = cache.compactions
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
@@ -487,6 +540,7 @@ def main():
     ev1.record()
     torch.cuda.synchronize()
     launches = lib.rkv_launch_count() - launches0
+    timed_compactions = cache.compactions - compactions0
     timer.enabled = False
     clock_info = clocks.stop() if clocks else None
     ms = ev0.elapsed_time(ev1)
@@ -584,6 +638,8 @@ def main():
                "copies": "pinned host buffers; step s+1 up and step s down on two copy "
                          "streams while step s decodes (double-buffered)"}
 
+    # device-side errors of every launch above (bounded waits, page ids) surface here
+    cache.check_errors()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -620,11 +676,19 @@ def main():
             "frac": achieved / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
             "kernel": "rkv::sm100::decode_kernel (score+attend, and attend-only on compaction steps)",
             "launches": n_launch, "kernel_ms_total": kern_ms,
+            "event_bracket": "each bracket holds the decode launch, its merge launch and the "
+                             "gap to the next launch (an event also ends the programmatic "
+                             "overlap of consecutive launches), so achieved is a lower bound "
+                             "on the kernel's own rate",
             "timed_launches": f"CUDA events around each decode launch of every {timer.every}-th "
                               f"timed step ({n_launch} of {timer.all_launches} launches)",
             "traffic": (tpb * kern_bytes / n_launch) if (tpb and n_launch) else None,
         },
         "gpu_launches": int(launches),
+        "compactions_timed": int(timed_compactions),
+        "compactions_note": f"{timed_compactions} layer compactions in the {args.steps} timed "
+                            f"steps x {len(layers)} layers (steady state: ~1 in 20-85 "
+                            f"layer-steps, by layer depth)",
         "prefill_s": prefill_s,
         "host_enqueue_ms_per_step": host_ms / args.steps,
         "e2e": e2e,
@@ -632,8 +696,11 @@ def main():
     }
     if world == 1 and not args.no_cpu_baseline:
         try:
-            res = oracle_sample(w, steps=2, warmup=0, threads=os.cpu_count())
+            del inputs
+            res = oracle_sample(w, steps=2, warmup=0, threads=os.cpu_count(), parity_dev=dev)
             line["cpu_baseline"] = {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")}
+            line["cpu_baseline"]["ms_per_step_extrapolated"] = res["ms_per_step_est"]
+            line["parity"] = res.get("parity")
         except Exception as exc:  # report, never hide
             line["cpu_baseline"] = {"error": repr(exc)}
     print(json.dumps(line), flush=True)

@@ -147,7 +147,10 @@ int rkv_decode_attention(const rkv_query* q, const rkv_kv_layout* kv, float scal
  * Its scratch is a fixed RKV_NOALLOC_SCRATCH_BYTES array built into the library, held on
  * every device that loads it; calls needing more return RKV_ERR_WORKSPACE_TOO_SMALL without
  * launching.  The first call on a device looks up the array's device address, so make it
- * before any stream capture.  All calls share the array: calls that overlap on the GPU race. */
+ * before any stream capture.  All calls share the array: calls that overlap on the GPU race.
+ * Device-side errors (a bounded wait that gave up, a page id outside the storage) are not
+ * reported by this entry point: they land in an error flag inside the array that nothing
+ * reads back; use rkv_decode_attention with a readable workspace when they matter. */
 #define RKV_NOALLOC_SCRATCH_BYTES (16u << 20)
 int rkv_decode_attention_noalloc(const rkv_query* q, const rkv_kv_layout* kv, float scale,
                                  int causal, const rkv_output* out, void* stream);

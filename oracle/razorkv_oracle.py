@@ -252,6 +252,9 @@ class OracleCache:
         self.next_id: List[int] = []
         self.seen = 0
         self.decisions: List[Decision] = []
+        # kept_override(layer, decision index, kept, margin) -> replacement kept pages or None
+        # (lets a test follow another implementation's decision at a provable near-tie)
+        self.kept_override = None
 
     def _init_salience(self, k):
         if self.cfg.salience_init == "norm":
@@ -299,6 +302,10 @@ class OracleCache:
         k = max(1, min(num_pages, hb // P))
         avg = batch_mean(scores)
         kept, margin = canonical_topk(avg, k)
+        if self.kept_override is not None:
+            repl = self.kept_override(layer, len(self.decisions), kept, margin)
+            if repl is not None:
+                kept = np.asarray(repl, dtype=np.int64)
         tok = (hs + kept[:, None] * P + np.arange(P)[None, :]).reshape(-1)
         parts = [np.arange(0, sink), tok]
         if aligned < he - hs:

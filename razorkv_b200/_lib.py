@@ -123,6 +123,21 @@ class RazorKVError(RuntimeError):
     pass
 
 
+# Codes a decode kernel leaves in a workspace's error flag (read by Workspace.check_errors).
+DEVICE_ERRORS = {
+    1: "a bounded wait inside a decode kernel gave up (the launch's output is incomplete)",
+    2: "a page-table entry lies outside the page pool (that page was read as slot 0)",
+}
+
+
+class DeviceError(RazorKVError):
+    """A device-side error that a decode kernel recorded in its workspace flag."""
+
+    def __init__(self, code: int):
+        self.code = code
+        super().__init__(f"device error {code}: {DEVICE_ERRORS.get(code, 'unknown code')}")
+
+
 def check(status: int, what: str):
     if status != 0:
         raise RazorKVError(f"{what}: {_STATUS.get(status, status)} (status {status})")

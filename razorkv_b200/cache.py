@@ -87,6 +87,20 @@ class RazorLayerState:
         self.cumulative_length = max(0, self.cumulative_length - tokens_to_remove)
 
 
+class SelectionRecord:
+    """One compaction decision of a layer (``PagedRazorKVCache.record_decisions``).
+
+    ``kept`` (ascending haystack page indices, int64) and ``margin`` (one fp32: the k-th minus
+    the (k+1)-th largest batch-mean page score, +inf when every page is kept) stay on the
+    device until read."""
+
+    __slots__ = ("layer", "seq_len", "budget", "kind", "num_pages", "k", "kept", "margin")
+
+    def __init__(self, layer, seq_len, budget, kind, num_pages=0, k=0, kept=None, margin=None):
+        self.layer, self.seq_len, self.budget, self.kind = layer, seq_len, budget, kind
+        self.num_pages, self.k, self.kept, self.margin = num_pages, k, kept, margin
+
+
 class PagedKV:
     """The K (which=0) or V (1) of one layer as ``update`` returns it on decode steps when
     ``return_handles`` is set: nothing is gathered; ``materialize()`` gives the contiguous
@@ -166,8 +180,13 @@ class PagedRazorKVCache(BaseCacheClass):
         self._layers: List[RazorLayerState] = []
         # selection hooks / diagnostics
         self.score_reducer: Optional[Callable[[torch.Tensor], torch.Tensor]] = None
-        self.record_margins = False
-        self.margins: List[Tuple[int, torch.Tensor]] = []
+        # with record_decisions set, every compaction appends a SelectionRecord (device
+        # tensors, read when the caller syncs); kept_override(layer, index, kept, margin) may
+        # return a replacement kept-page tensor (to follow an external decision trace)
+        self.compactions = 0   # compactions run so far (all layers; prefill ones included)
+        self.record_decisions = False
+        self.decisions: List["SelectionRecord"] = []
+        self.kept_override: Optional[Callable[[int, int, torch.Tensor], Optional[torch.Tensor]]] = None
         # decode steps of ``update`` return PagedKV handles instead of gathered K/V; the
         # engine's attention function then reads the pool directly
         self.return_handles = False
@@ -438,6 +457,9 @@ class PagedRazorKVCache(BaseCacheClass):
             return
         hb = target_budget - sink - local
         if hb <= 0:
+            self.compactions += 1
+            if self.record_decisions:
+                self.decisions.append(SelectionRecord(layer_idx, N, target_budget, "zones"))
             self._compact_copy(layer_idx, new_len=sink + local, sink=sink, kept=None, k=0,
                                hay_start=hs, tail_src_start=he)
             return
@@ -445,7 +467,15 @@ class PagedRazorKVCache(BaseCacheClass):
         if num_pages <= 0:
             return
         k = max(1, min(num_pages, hb // P))
-        kept = self._select(layer_idx, hs, num_pages, k)
+        self.compactions += 1
+        kept, margin = self._select(layer_idx, hs, num_pages, k)
+        if self.kept_override is not None:
+            repl = self.kept_override(layer_idx, len(self.decisions), kept, margin)
+            if repl is not None:
+                kept = repl.to(device=self._device, dtype=torch.int64).contiguous()
+        if self.record_decisions:
+            self.decisions.append(SelectionRecord(layer_idx, N, target_budget, "pages", num_pages,
+                                                  k, kept.clone(), margin))
         aligned_end = hs + num_pages * P
         new_len = sink + k * P + (N - aligned_end)
         if hs % P == 0:
@@ -479,9 +509,7 @@ class PagedRazorKVCache(BaseCacheClass):
                                   kept.data_ptr(), margin.data_ptr(), ws.data_ptr(), ws.numel(),
                                   self._stream())
         check(st, "rkv_select_pages")
-        if self.record_margins:
-            self.margins.append((layer_idx, margin))
-        return kept
+        return kept, margin
 
     def _compact_copy(self, layer_idx, new_len, sink, kept, k, hay_start, tail_src_start):
         lib = _lib.load()
@@ -678,6 +706,13 @@ class PagedRazorKVCache(BaseCacheClass):
         self._seen_tokens = seen
         self._layers[layer_idx].cumulative_length = seen
         return out
+
+    def check_errors(self) -> None:
+        """Raise ``DeviceError`` if a decode kernel of this cache's device recorded a
+        device-side error (a bounded wait that gave up, a page id outside the pool) since the
+        last check, and clear the flags.  Synchronises the device."""
+        if self._device is not None:
+            Workspace.check_errors(self._device)
 
     def _kv_bytes(self, layer_idx: int) -> int:
         """Bytes of retained K and V one attention pass over the layer reads."""

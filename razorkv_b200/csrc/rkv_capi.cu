@@ -66,6 +66,7 @@ AttnParams attn_params(const rkv_query* q, const rkv_kv_layout* kv, float scale,
     p.stride_b = kv->stride_b; p.stride_h = kv->stride_h; p.stride_p = kv->stride_p;
     p.stride_t = kv->stride_t; p.page_size = kv->page_size;
     p.page_table = kv->page_table; p.pt_stride_b = kv->pt_stride_b;
+    p.num_slots = kv->page_table ? kv->num_slots : 0;
     p.scale = scale > 0.0f ? scale : (float)(1.0 / sqrt((double)kv->head_dim));
     p.causal = causal;
     p.out = out->out; p.out_dtype = out->dtype;
@@ -105,6 +106,18 @@ FusedParams fused_params(const rkv_query* q, const rkv_kv_layout* kv, const rkv_
 
 }  // namespace
 
+namespace rkv {
+// The argument checks rkv_decode_attention makes before it touches the workspace (shared with
+// the no-allocation entry point, which must reject a call before it queues any work).
+int attention_args_status(const rkv_query* q, const rkv_kv_layout* kv, const rkv_output* out) {
+    int st = check_kv(kv, true);
+    if (st) return st;
+    if ((st = check_q(q, kv))) return st;
+    if (!out || !out->out || !dtype_ok(out->dtype)) return RKV_ERR_INVALID_ARGUMENT;
+    return RKV_OK;
+}
+}  // namespace rkv
+
 extern "C" {
 
 const char* rkv_status_string(int s) {
@@ -143,10 +156,8 @@ size_t rkv_decode_attention_workspace_size(const rkv_query* q, const rkv_kv_layo
 int rkv_decode_attention(const rkv_query* q, const rkv_kv_layout* kv, float scale, int causal,
                          const rkv_output* out, void* workspace, size_t workspace_bytes,
                          void* stream) {
-    int st = check_kv(kv, true);
+    int st = attention_args_status(q, kv, out);
     if (st) return st;
-    if ((st = check_q(q, kv))) return st;
-    if (!out || !out->out || !dtype_ok(out->dtype)) return RKV_ERR_INVALID_ARGUMENT;
     if (kv->batch == 0) return RKV_OK;
     if (workspace_bytes < rkv_decode_attention_workspace_size(q, kv) || !workspace)
         return RKV_ERR_WORKSPACE_TOO_SMALL;

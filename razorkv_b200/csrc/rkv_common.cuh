@@ -62,14 +62,18 @@ __device__ __forceinline__ float key_to_float(uint32_t k) {
 // Location of logical token t of one (sequence, kv-head) plane.
 //   page_table == nullptr : contiguous rows, element offset t * stride_t
 //   otherwise             : page page_table[t / P] (times stride_p) plus (t % P) * stride_t
+//   num_slots > 0         : a page id outside [0, num_slots) reads physical page 0 instead
+//                           (a caller's table is never trusted to stay inside the storage)
 struct TokenMap {
     const int64_t* page_table;   // [.., n_pages] int64; row for this sequence already applied
     int64_t page_size;
     int64_t stride_p;            // elements between physical pages
     int64_t stride_t;            // elements between tokens inside a page
+    int64_t num_slots = 0;       // physical pages in the storage (0: ids not checked)
     __device__ __forceinline__ int64_t offset(int64_t t) const {
         if (page_table == nullptr) return t * stride_t;
         int64_t pg = page_table[t / page_size];
+        if (num_slots > 0 && (pg < 0 || pg >= num_slots)) pg = 0;
         return pg * stride_p + (t % page_size) * stride_t;
     }
 };

@@ -141,7 +141,7 @@ attn_split_kernel(AttnParams p) {
     }
     float m = -INFINITY, l = 0.0f;
     TokenMap tm{p.page_table ? p.page_table + (int64_t)b * p.pt_stride_b : nullptr,
-                p.page_size, p.stride_p, p.stride_t};
+                p.page_size, p.stride_p, p.stride_t, p.num_slots};
     const int64_t base = (int64_t)b * p.stride_b + (int64_t)kvh * p.stride_h;
     for (int64_t t = s0; t < s1; ++t) {
         const int64_t off = base + tm.offset(t);

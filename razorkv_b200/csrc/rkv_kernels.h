@@ -30,7 +30,7 @@ struct AttnParams {
     int Hq, QL;
     const void* k; const void* v; int kv_dtype; int D; int Hkv; int64_t B, N;
     int64_t stride_b, stride_h, stride_p, stride_t, page_size;
-    const int64_t* page_table; int64_t pt_stride_b;
+    const int64_t* page_table; int64_t pt_stride_b; int64_t num_slots;
     float scale; int causal;
     void* out; int out_dtype; int64_t o_stride_b, o_stride_h, o_stride_t;
     float* workspace; int num_splits;

@@ -12,15 +12,28 @@
 // name as a device address (on the host it names a host-side stand-in), so the first call on
 // each device looks up the real device address with cudaGetSymbolAddress while that device is
 // current and keeps it; make that first call before any stream capture.  The array is shared
-// by every call on the device and keeps the previous call's contents, so each call clears the
-// part that must start at zero (the workspace header: error flag and merge counters) on its
-// stream before launching.  Calls whose kernels overlap on the GPU (different streams, or
-// different host threads) race on the array; serialise them.
+// by every call on the device and keeps the previous call's contents, so each valid call
+// clears, on its stream and before its launch, the part that must start at zero: the error
+// flag word and the merge counters of its batch.  That clear is a small memset between two
+// decode launches, so consecutive calls do not overlap a launch's start with the previous
+// one's tail as rkv_decode_attention with a caller workspace does.  Calls whose kernels
+// overlap on the GPU (different streams, or different host threads) race on the array;
+// serialise them.
+//
+// Device-side errors are not reported here.  The decode kernels record a bounded wait that
+// gave up, or a page id outside the storage, in the error flag inside the scratch array,
+// which no entry point reads back, and the next call clears it.  A caller that needs those
+// errors uses rkv_decode_attention with a workspace it can read (its first int32, at
+// rkv_workspace_error_flag_offset()).
 #include <cuda_runtime.h>
 
 #include <mutex>
 
 #include "../../include/razorkv_b200.h"
+
+namespace rkv {
+int attention_args_status(const rkv_query* q, const rkv_kv_layout* kv, const rkv_output* out);
+}
 
 namespace {
 
@@ -49,14 +62,19 @@ int scratch_address(void** out) {
 extern "C" int rkv_decode_attention_noalloc(const rkv_query* q, const rkv_kv_layout* kv,
                                             float scale, int causal, const rkv_output* out,
                                             void* stream) {
-    if (!q || !kv || !out) return RKV_ERR_INVALID_ARGUMENT;
+    // reject a bad call before anything is queued
+    int st = rkv::attention_args_status(q, kv, out);
+    if (st) return st;
+    if (kv->batch == 0) return RKV_OK;
     const size_t need = rkv_decode_attention_workspace_size(q, kv);
     if (need > (size_t)RKV_NOALLOC_SCRATCH_BYTES) return RKV_ERR_WORKSPACE_TOO_SMALL;
     void* ws = nullptr;
-    int st = scratch_address(&ws);
+    st = scratch_address(&ws);
     if (st) return st;
-    if (cudaMemsetAsync(ws, 0, RKV_WORKSPACE_HEADER_BYTES, static_cast<cudaStream_t>(stream)) !=
-        cudaSuccess)
+    // error flag [0, 4) and the per-sequence merge counters [256, 256 + 4 B) of the header
+    const size_t clear = 256 + 4 * (size_t)kv->batch;
+    if (cudaMemsetAsync(ws, 0, clear < RKV_WORKSPACE_HEADER_BYTES ? clear : RKV_WORKSPACE_HEADER_BYTES,
+                        static_cast<cudaStream_t>(stream)) != cudaSuccess)
         return RKV_ERR_CUDA;
     return rkv_decode_attention(q, kv, scale, causal, out, ws, (size_t)RKV_NOALLOC_SCRATCH_BYTES,
                                 stream);

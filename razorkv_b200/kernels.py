@@ -32,6 +32,7 @@ __all__ = [
     "compacted_paged_sdpa",
     "compute_page_salience_pool",
     "is_triton_available",
+    "check_device_errors",
     "Workspace",
 ]
 
@@ -43,6 +44,8 @@ class Workspace:
     kernels return them to zero after every launch)."""
 
     _pool = {}
+    # error flags of workspaces replaced by larger ones (read by the next check)
+    _retired = {}
 
     @classmethod
     def get(cls, device: torch.device, nbytes: int) -> torch.Tensor:
@@ -52,9 +55,53 @@ class Workspace:
             size = max(nbytes, 1 << 20)
             if buf is not None:
                 size = max(size, 2 * buf.numel())
+                # keep the old flag word until it has been checked
+                cls._retired.setdefault(device.index, []).append(cls._flag(buf).clone())
             buf = torch.zeros(size, dtype=torch.uint8, device=device)
             cls._pool[key] = buf
         return buf
+
+    @staticmethod
+    def _flag(buf: torch.Tensor) -> torch.Tensor:
+        off = int(_lib.load().rkv_workspace_error_flag_offset())
+        return buf[off: off + 4].view(torch.int32)
+
+    @classmethod
+    def check_errors(cls, device=None, clear: bool = True) -> None:
+        """Raise ``DeviceError`` if a decode kernel flagged an error in any workspace of
+        ``device`` (all devices when None) since the last check, and clear the flags.
+
+        The decode kernels never stop the stream on a device-side error: a bounded wait that
+        gave up (code 1) or a page-table entry outside the pool (code 2; the page is read as
+        slot 0 instead) only sets the workspace's int32 error flag, so the result of that
+        launch is wrong while the launch itself reports success.  This check reads the flags
+        (one device synchronisation), so call it at sync points -- after a generation, at the
+        end of a timed region, in tests -- not inside the decode loop."""
+        codes = []
+        for (dev, _), buf in list(cls._pool.items()):
+            if device is not None and dev != torch.device(device).index:
+                continue
+            flag = cls._flag(buf)
+            code = int(flag.item())
+            if code:
+                codes.append(code)
+                if clear:
+                    flag.zero_()
+        for dev in list(cls._retired):
+            if device is not None and dev != torch.device(device).index:
+                continue
+            codes += [int(f.item()) for f in cls._retired[dev] if int(f.item())]
+            if clear:
+                del cls._retired[dev]
+        if codes:
+            raise _lib.DeviceError(max(codes))
+
+
+def check_device_errors(device=None) -> None:
+    """Raise ``razorkv_b200._lib.DeviceError`` if a decode kernel recorded a device-side
+    error on ``device`` (every device when None) since the last check; clears the flags.
+    Synchronises the device: call it at sync points, not per step."""
+    Workspace.check_errors(device)
 
 
 def _query(q: torch.Tensor) -> Query:

@@ -56,3 +56,42 @@ def iter_inputs(case, device="cpu"):
     for step in range(w.decode_steps):
         for layer in range(w.num_layers):
             yield "decode", step, layer, decode_inputs(w, step, layer, device)
+
+
+# Cases at the measured workloads' own scale.  Only a pair of layers of each model is run
+# (the shallowest and the deepest, with the budgets of the full model), for enough decode
+# steps that every layer compacts at least once after its prefill eviction.  Their fixtures
+# record the reference's top-k decisions (kept pages and the gap at the cut), a strided
+# sample of the final salience and the attention output of the last step, not every tensor.
+SCALE_CASES = {
+    # Llama-3.1-8B shape: batch 8, 32/8 heads, d128, bf16, 32768-token prefill, linear
+    # pyramid 15 % -> 70 %; layer 31 first compacts at decode step 85
+    "llama8b_b8_32k_l0_l31": dict(workload=WORKLOADS["llama8b-b8-32k-bf16"], layers=(0, 31),
+                                  decode_steps=86, query=True),
+    # Qwen-2.5-7B shape: batch 1, 28/4 heads (GQA 7), d128, bf16, 131072-token prefill
+    # (8192 pages); layer 27 first compacts at decode step 74
+    "qwen7b_b1_128k_l0_l27": dict(workload=WORKLOADS["qwen7b-b1-128k-bf16"], layers=(0, 27),
+                                  decode_steps=75, query=True),
+}
+
+# salience sample stride of the scale fixtures (tokens)
+SCALE_SAL_STRIDE = 7
+
+
+def iter_scale_inputs(case, device="cpu", steps=None):
+    """As ``iter_inputs`` for the selected layers of a scale case (real layer indices)."""
+    w = case["workload"]
+    for layer in case["layers"]:
+        yield "prefill", -1, layer, layer_prefill(w, layer, device)
+    n = case["decode_steps"] if steps is None else steps
+    for step in range(n):
+        for layer in case["layers"]:
+            yield "decode", step, layer, decode_inputs(w, step, layer, device)
+
+
+def scale_input_digest(sha, kind, tensors):
+    """Adds a cheap digest of one step's inputs: prefill K/V every 61st token, all else."""
+    for i, t in enumerate(tensors):
+        if kind == "prefill" and i < 2:
+            t = t[:, :, ::61]
+        sha.update(t.float().contiguous().numpy().tobytes())

@@ -58,3 +58,39 @@ def run_oracle(name):
         ids[layer].append(cache.ids[layer].copy())
     return {"input_sha": sha.digest(), "out": np.stack(outs), "ids": ids,
             "sal": [s.copy() for s in cache.S], "decisions": cache.decisions, "cache": cache}
+
+
+# ---- scale cases ------------------------------------------------------------------------------
+def load_scale(name):
+    """Reads a scale fixture: the reference's decisions, final lengths, salience sample and
+    last-step outputs (see tests/golden/make_golden.py, run_reference_scale_case)."""
+    from tests.golden.cases import SCALE_CASES
+    z = np.load(os.path.join(GOLDEN_DIR, f"{name}.npz"))
+    off = z["kept_off"]
+    decisions = []
+    for i in range(len(off) - 1):
+        decisions.append(dict(layer=int(z["dec_layer"][i]), step=int(z["dec_step"][i]),
+                              seq_len=int(z["dec_seq_len"][i]), budget=int(z["dec_budget"][i]),
+                              num_pages=int(z["dec_num_pages"][i]), k=int(z["dec_k"][i]),
+                              margin=float(z["dec_margin"][i]),
+                              kept=z["kept"][off[i]:off[i + 1]].astype(np.int64)))
+    layers = SCALE_CASES[name]["layers"]
+    return {"input_sha": bytes(z["input_sha"]), "decisions": decisions,
+            "len": {l: int(z[f"len_{l}"]) for l in layers},
+            "sal": {l: z[f"sal_{l}"] for l in layers},
+            "out": {l: z[f"out_{l}"] for l in layers}}
+
+
+def near_tie(margin, score_scale):
+    """True when a top-k cut is close enough to a tie that two fp32 summation orders may
+    legitimately disagree on it: the gap at the cut is within 4e-6 of the largest salience
+    (~34 ulps; the canonical order and torch's differ by <= 5e-7 relative on salience)."""
+    return abs(margin) <= 4e-6 * max(abs(score_scale), 1.0)
+
+
+def oracle_config(w):
+    from oracle import razorkv_oracle as O
+    return O.OracleConfig(compression_ratio=w.compression_ratio, sink_tokens=w.sink_tokens,
+                          local_window=w.local_window, page_size=w.page_size,
+                          pyramid_mode=w.pyramid_mode, pyramid_min_ratio=w.pyramid_min_ratio,
+                          pyramid_max_ratio=w.pyramid_max_ratio)
