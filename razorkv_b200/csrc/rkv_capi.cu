@@ -144,8 +144,11 @@ int rkv_selftest_wait_timeout(int* result, long long limit_cycles, void* stream)
 }
 
 size_t rkv_decode_attention_workspace_size(const rkv_query* q, const rkv_kv_layout* kv) {
-    if (!q || !kv) return 0;
-    const int64_t G = q->num_heads / (kv->num_kv_heads > 0 ? kv->num_kv_heads : 1);
+    // sizes of a call rkv_decode_attention would reject: no workspace can make it valid
+    if (!q || !kv || kv->num_kv_heads < 1 || kv->batch < 0 || kv->num_tokens < 0 ||
+        q->num_heads < 1 || q->q_len < 1 || kv->head_dim < 1 || kv->head_dim > kMaxHeadDim)
+        return 0;
+    const int64_t G = q->num_heads / kv->num_kv_heads;
     int splits = attn_num_splits(kv->num_tokens, kv->batch, kv->num_kv_heads, G * q->q_len);
     size_t generic = attn_workspace_floats(kv->batch, q->num_heads, q->q_len, kv->head_dim, splits) *
                      sizeof(float);
@@ -189,7 +192,7 @@ int rkv_append(const rkv_kv_layout* kv, const rkv_salience* sal, const void* k_n
     int st = check_kv(kv, true);
     if (st) return st;
     if (!sal || !sal->s || !k_new || !v_new || !page_table || !free_stack) return RKV_ERR_INVALID_ARGUMENT;
-    if (n_new < 0 || pos < 0 || free_top < 0) return RKV_ERR_INVALID_ARGUMENT;
+    if (n_new < 0 || pos < 0 || free_top < 0 || kv->page_size < 1) return RKV_ERR_INVALID_ARGUMENT;
     const int64_t P = kv->page_size;
     const int64_t first_new = (pos + P - 1) / P;
     const int64_t last_page = (pos + n_new + P - 1) / P;   // exclusive

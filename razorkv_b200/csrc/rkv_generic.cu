@@ -602,6 +602,7 @@ cudaError_t launch_score(const ScoreParams& p, cudaStream_t st) {
 int attn_num_splits(int64_t N, int64_t B, int64_t Hkv, int64_t rows) {
     // aim for ~4 CTAs per SM over 148 SMs; at least 16 tokens per split
     int64_t ctas = B * Hkv * ((rows + kAttnWarps - 1) / kAttnWarps);
+    if (ctas <= 0) return 1;
     int64_t want = (148 * 4 + ctas - 1) / ctas;
     int64_t maxs = (N + 15) / 16;
     if (want > maxs) want = maxs;

@@ -47,3 +47,30 @@ def test_argument_errors_without_a_device():
     assert lib.rkv_compact_pages(None, 0, 1, None, 1, 1, 1, None, 0, None) == 1
     assert lib.rkv_release_pages(None, 3, None, 0, None) == 1
     assert lib.rkv_page_salience_pool(None, 1, 8, 8, 4, 0, None, None) == 1
+
+
+def test_zeroed_structures_are_rejected_not_crashed():
+    """Every struct-taking entry point and size query survives zeroed or inconsistent
+    structures (zero heads, zero page size, null pointers) and reports an error status or a
+    zero size, without reaching CUDA."""
+    lib = _lib.load()
+    lay, q, o, s = _lib.KVLayout(), _lib.Query(), _lib.Output(), _lib.Salience()
+    assert lib.rkv_decode_attention_workspace_size(q, lay) == 0
+    assert lib.rkv_decode_fused_workspace_size(q, lay) == 0
+    assert lib.rkv_decode_scored_workspace_size(q, lay) == 0
+    assert lib.rkv_decode_attention(q, lay, 0.0, 0, o, None, 0, None) != 0
+    assert lib.rkv_decode_attention_noalloc(q, lay, 0.0, 0, o, None) != 0
+    assert lib.rkv_decode_fused(q, lay, s, 0.98, 0.02, 0.0, o, None, 0, None) != 0
+    assert lib.rkv_decode_scored(q, q, lay, s, 0, 0.98, 0.02, 0.0, o, None, 0, None) != 0
+    assert lib.rkv_append_decode(lay, s, None, None, 0, 0, None, None, 0, 0, q, 0.98, 0.02, 0.0,
+                                 o, None, 0, None) != 0
+    assert lib.rkv_score(q, lay, s, 0.98, 0.02, 1, None) != 0
+    assert lib.rkv_gather_tokens(lay, 0, None, None, None, None) != 0
+    assert lib.rkv_page_scores(lay, s, 0, 1, 16, None, None) != 0
+    # a plausible layout whose page size is zero
+    lay.k, lay.v, lay.dtype, lay.head_dim, lay.batch, lay.num_kv_heads = 16, 16, 2, 128, 1, 2
+    assert lib.rkv_append(lay, s, 16, 16, 0, 0, 0, 1, 0, 16, 16, 4, 0, None) == 1
+    q.q, q.dtype, q.num_heads, q.q_len = 16, 2, 3, 1   # 3 query heads over 2 kv heads
+    assert lib.rkv_decode_attention_workspace_size(q, lay) > 0
+    o.out, o.dtype = 16, 2
+    assert lib.rkv_decode_attention(q, lay, 0.0, 0, o, None, 0, None) == 1
