@@ -74,9 +74,18 @@ AttnParams attn_params(const rkv_query* q, const rkv_kv_layout* kv, float scale,
     return p;
 }
 
+// The screened instances (5-8 query heads per kv head) read query rows of the scoring query
+// with 16-byte loads: its base and head / sequence strides must keep rows 16-byte aligned.
+bool q_rows_aligned(const rkv_query* q) {
+    const int64_t eb = q->dtype == RKV_F32 ? 4 : 2;
+    return !(reinterpret_cast<uintptr_t>(q->q) & 15) && (q->stride_b * eb) % 16 == 0 &&
+           (q->stride_h * eb) % 16 == 0;
+}
+
 bool fast_ok(const rkv_query* q, const rkv_kv_layout* kv, bool need_v) {
     if (q->q_len != 1) return false;
     if (!kv->page_table) return false;
+    if (q->num_heads / kv->num_kv_heads > 4 && !q_rows_aligned(q)) return false;
     return fused_supported(kv->dtype, kv->head_dim, (int)kv->num_kv_heads, q->num_heads,
                            kv->page_size, kv->stride_t, kv->stride_h, kv->stride_b,
                            kv->stride_p, kv->k, need_v ? kv->v : kv->k) &&
@@ -291,7 +300,8 @@ int rkv_decode_scored(const rkv_query* q_score, const rkv_query* q_attn, const r
     if (kv->batch == 0) return RKV_OK;
     if (workspace_bytes < rkv_decode_scored_workspace_size(q_attn, kv) || !workspace)
         return RKV_ERR_WORKSPACE_TOO_SMALL;
-    if (kv->num_tokens > 0 && fast_ok(q_attn, kv, true) && q_score->dtype == q_attn->dtype) {
+    if (kv->num_tokens > 0 && fast_ok(q_attn, kv, true) && q_score->dtype == q_attn->dtype &&
+        (q_score->num_heads / kv->num_kv_heads <= 4 || q_rows_aligned(q_score))) {
         FusedParams p = fused_params(q_score, kv, sal, decay, one_minus_decay, scale, out);
         p.q2 = q_attn->q; p.q2_stride_b = q_attn->stride_b; p.q2_stride_h = q_attn->stride_h;
         p.has_score_n = 1; p.score_n = score_tokens;

@@ -198,6 +198,49 @@ __device__ __forceinline__ int head_of_lane(int j) {
     return GP == 8 ? j : GP == 4 ? (j >> 1) : GP == 2 ? (j >> 2) : 0;
 }
 
+// Screened resonance (instances with 5-8 query heads per kv head).  The resonance of a token
+// is the max over its G query heads of the canonical fp32 dot fl(q*scale_r).k; only the max
+// matters.  Every head's dot is first taken on tensor cores (x_h, fp32 accumulate, order not
+// specified) together with A_h = |q_h|.|k| from a second mma on the magnitudes.  With
+//   E_h = kScreenTol * scale_r * A_h,   kScreenTol = 2^-14,
+// |scale_r * x_h - canonical_h| <= E_h holds with a wide margin: the canonical chains round
+// at most ~14 times (<= 2^-19.8 relative to scale_r * A_h) and a tensor-core fp32 sum of
+// exact bf16/fp16 products stays within a few ulps of its largest partial sum (<= 2^-19
+// relative to A_h for 128 terms).  A head h whose upper bound scale_r * x_h + E_h lies below
+// LB = max_j (scale_r * x_j - E_j) cannot hold the maximum, since its canonical value is
+// below that of the head attaining LB; the canonical dot is computed only for the remaining
+// candidates (usually one head), so the resonance is the same bit pattern as the full
+// canonical max over all heads.  Non-finite values keep a head a candidate.
+constexpr float kScreenTol = 6.103515625e-05f;   // 2^-14
+constexpr uint32_t kAbsMask2 = 0x7fff7fffu;       // clears the sign of both bf16/fp16 halves
+
+__device__ __forceinline__ uint4 ldg128(const void* p) {
+    return __ldg(reinterpret_cast<const uint4*>(p));
+}
+
+// Canonical-order dot of K row t of the staged page (128-byte swizzled halves at kb) with
+// fl(q_row * scale): lane j of each 8-lane group owns chunk j of every 64-element half; two
+// FMA chains (even / odd element positions) from +0.0f; xor-4/2/1 butterfly.  Every lane of
+// the group returns the same value.  q_row must be 16-byte aligned.
+template <typename T, int HALVES>
+__device__ __forceinline__ float canon_row_dot(uint32_t kb, int half_bytes, int t,
+                                               const T* q_row, int j, float scale) {
+    uint64_t kp[HALVES * 4], qp[HALVES * 4];
+#pragma unroll
+    for (int hf = 0; hf < HALVES; ++hf) {
+        unpack8_pairs<T>(lds128(kb + hf * half_bytes + t * 128 + ((j ^ (t & 7)) << 4)), kp + hf * 4);
+        float f[8];
+        unpack8<T>(ldg128(q_row + hf * 64 + 8 * j), f);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            qp[hf * 4 + i] = pack2(__fmul_rn(f[2 * i], scale), __fmul_rn(f[2 * i + 1], scale));
+    }
+    uint64_t x = 0ull;   // (+0.0f, +0.0f)
+#pragma unroll
+    for (int e = 0; e < HALVES * 4; ++e) ffma2(x, qp[e], kp[e]);
+    return group8_sum(sum_pair(x));
+}
+
 // MODE 0: one query; its canonical-order scores give the resonance and the attention logits.
 // MODE 1: attention only; the logits come from mma.sync (K tile x q^T, fp32 accumulate).
 // MODE 2: two queries: the canonical-order scores of q (resonance, tokens before score_n)
@@ -211,6 +254,9 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
     constexpr int EPL = D / 8;          // K elements a lane owns per row
     constexpr int MT = D / 16;          // 16-dim mma row tiles
     constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+    // 5-8 query heads per kv head: resonance by the tensor-core screen (see kScreenTol) and
+    // attention logits on tensor cores, as in MODE 1
+    constexpr bool SCREEN = GP == 8 && MODE != 1;
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -432,8 +478,12 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
     const bool head_writer = (j & ((8 / GP) - 1)) == 0;   // one lane per head in each group
     const uint32_t ps_base = smem_u32(&sm.ps[warp][0][0]);
 
-    uint64_t qreg[GP][EPL / 2];   // MODE 0 / 2: fl(q * scale) as (even, odd) element pairs
-    uint32_t qf[D / 16][2];       // MODE 1 / 2: q2^T as mma B fragments (bf16 / fp16 pairs)
+    // MODE 0 / 2 without the screen: fl(q * scale) as (even, odd) element pairs
+    uint64_t qreg[SCREEN ? 1 : GP][EPL / 2];
+    uint32_t qf[D / 16][2];       // MODE 1 / 2 and screened MODE 0: q2^T as mma B fragments
+    // screened MODE 2: the score query's fragments; screened modes: their magnitudes
+    uint32_t qsf[(SCREEN && MODE == 2) ? D / 16 : 1][2];
+    uint32_t qa[SCREEN ? D / 16 : 1][2];
     float acc[MT][4];
     int slot = 0;
     uint32_t par = 0;
@@ -442,7 +492,22 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
         const int64_t seg_end = min(r1, (b + 1) * a.n_tiles);
         const int64_t tb0 = pos - b * a.n_tiles, tb1 = seg_end - b * a.n_tiles;
 
-        if constexpr (MODE != 1) {
+        if constexpr (SCREEN) {
+            // B fragments of the score query q (MODE 2) and of the magnitudes of whichever
+            // query scores (q in both modes: in MODE 0 the attention query is q itself)
+            const int n = lane >> 2;
+            const T* qr = static_cast<const T*>(a.q) + b * a.q_stride_b + (int64_t)(h * G + n) * a.q_stride_h;
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+                const int d0 = kk * 16 + 2 * (lane & 3);
+                const uint32_t f0 = n < G ? pack_elems<T>(qr[d0], qr[d0 + 1]) : 0u;
+                const uint32_t f1 = n < G ? pack_elems<T>(qr[d0 + 8], qr[d0 + 9]) : 0u;
+                if constexpr (MODE == 2) { qsf[kk][0] = f0; qsf[kk][1] = f1; }
+                qa[kk][0] = f0 & kAbsMask2;
+                qa[kk][1] = f1 & kAbsMask2;
+            }
+        }
+        if constexpr (MODE != 1 && !SCREEN) {
             // fl(q * scale) for this lane's K elements: chunk j of every 64-element half
             const T* qb = static_cast<const T*>(a.q) + b * a.q_stride_b;
 #pragma unroll
@@ -457,9 +522,9 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                 }
             }
         }
-        if constexpr (MODE != 0) {
+        if constexpr (MODE != 0 || SCREEN) {
             // B = q2^T (dims x heads): lane holds head lane/4, dims 16kk + 2(lane%4) + {0,1}
-            // (b0) and the same + 8 (b1); heads past G are zero
+            // (b0) and the same + 8 (b1); heads past G are zero.  (q2 is q in MODE 0.)
             const int n = lane >> 2;
             const T* qr = static_cast<const T*>(a.q2) + b * a.q2_stride_b + (int64_t)(h * G + n) * a.q2_stride_h;
 #pragma unroll
@@ -528,9 +593,108 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                     if (lane == 0) sm.new_norm[slot][s][h] = nrm;
                 }
 
+                // attention logits in the mma accumulator layout (MODE 1 / 2 and screened
+                // MODE 0): tokens lane/4 and lane/4 + 8, heads 2(lane%4) and 2(lane%4) + 1
+                float c4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+
+                // ---- 1s. screened resonance (5-8 query heads per kv head) -----------------
+                if constexpr (SCREEN) {
+                    float cs[4] = {0.0f, 0.0f, 0.0f, 0.0f};   // score query . k
+                    float ca[4] = {0.0f, 0.0f, 0.0f, 0.0f};   // |score query| . |k|
+                    {
+                        const int mi = lane >> 3;
+                        const int tk = (lane & 7) + 8 * (mi & 1);
+#pragma unroll
+                        for (int kk = 0; kk < D / 16; ++kk) {
+                            const int c8 = (kk & 3) * 2 + (mi >> 1);
+                            uint32_t a0, a1, a2, a3;
+                            ldsm_x4(kb + (kk >> 2) * a.half_bytes + tk * 128 + ((c8 ^ (tk & 7)) << 4),
+                                    a0, a1, a2, a3);
+                            if constexpr (MODE == 2) {
+                                mma_16816<kBf16>(cs, a0, a1, a2, a3, qsf[kk][0], qsf[kk][1]);
+                                if (a.attend) mma_16816<kBf16>(c4, a0, a1, a2, a3, qf[kk][0], qf[kk][1]);
+                            } else {
+                                mma_16816<kBf16>(cs, a0, a1, a2, a3, qf[kk][0], qf[kk][1]);
+                            }
+                            mma_16816<kBf16>(ca, a0 & kAbsMask2, a1 & kAbsMask2, a2 & kAbsMask2,
+                                             a3 & kAbsMask2, qa[kk][0], qa[kk][1]);
+                        }
+                    }
+                    if constexpr (MODE == 0) {
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) c4[e] = cs[e];
+                    }
+                    if (a.score) {
+                        const int tA = lane >> 2, tB = tA + 8;
+                        const int nA = 2 * (lane & 3), nB = nA + 1;
+                        const int64_t gt = (int64_t)tile * kTileTokens;
+                        const bool vA = tA < nv && gt + tA < a.score_n;
+                        const bool vB = tB < nv && gt + tB < a.score_n;
+                        const bool ok[4] = {vA && nA < G, vA && nB < G, vB && nA < G, vB && nB < G};
+                        const float tol = a.scale_r * kScreenTol;
+                        float ap[4], eb[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            ap[e] = cs[e] * a.scale_r;
+                            eb[e] = ca[e] * tol;
+                        }
+                        // lower bound of each token's canonical max over its heads (the 8 heads
+                        // of a token sit in 4 consecutive lanes, 2 per lane)
+                        float lbA = fmaxf(ok[0] ? ap[0] - eb[0] : -INFINITY, ok[1] ? ap[1] - eb[1] : -INFINITY);
+                        float lbB = fmaxf(ok[2] ? ap[2] - eb[2] : -INFINITY, ok[3] ? ap[3] - eb[3] : -INFINITY);
+                        lbA = fmaxf(lbA, __shfl_xor_sync(0xffffffffu, lbA, 1));
+                        lbB = fmaxf(lbB, __shfl_xor_sync(0xffffffffu, lbB, 1));
+                        lbA = fmaxf(lbA, __shfl_xor_sync(0xffffffffu, lbA, 2));
+                        lbB = fmaxf(lbB, __shfl_xor_sync(0xffffffffu, lbB, 2));
+                        // candidate heads: upper bound not below the lower bound (NaN stays in)
+                        uint32_t mA = ((ok[0] && !(ap[0] + eb[0] < lbA)) ? 1u << nA : 0u) |
+                                      ((ok[1] && !(ap[1] + eb[1] < lbA)) ? 1u << nB : 0u);
+                        uint32_t mB = ((ok[2] && !(ap[2] + eb[2] < lbB)) ? 1u << nA : 0u) |
+                                      ((ok[3] && !(ap[3] + eb[3] < lbB)) ? 1u << nB : 0u);
+                        mA |= __shfl_xor_sync(0xffffffffu, mA, 1);
+                        mB |= __shfl_xor_sync(0xffffffffu, mB, 1);
+                        mA |= __shfl_xor_sync(0xffffffffu, mA, 2);
+                        mB |= __shfl_xor_sync(0xffffffffu, mB, 2);
+                        // canonical dots of the candidates: round r, group g takes token 4r + g
+                        // and its lowest candidate head; further candidates (rare) follow
+                        const T* qh0 = static_cast<const T*>(a.q) + b * a.q_stride_b +
+                                       (int64_t)(h * G) * a.q_stride_h;
+                        uint32_t keyr[4], rem[4];
+#pragma unroll
+                        for (int r = 0; r < 4; ++r) {
+                            const int t = 4 * r + g;
+                            const uint32_t msk = __shfl_sync(0xffffffffu, r < 2 ? mA : mB, (t & 7) * 4);
+                            const int hd = msk ? __ffs(msk) - 1 : 0;
+                            const float v = canon_row_dot<T, HALVES>(kb, a.half_bytes, t,
+                                                                     qh0 + (int64_t)hd * a.q_stride_h,
+                                                                     j, a.scale_r);
+                            keyr[r] = msk ? ordered_key(v) : 0u;
+                            rem[r] = msk & (msk - 1);
+                        }
+#pragma unroll
+                        for (int r = 0; r < 4; ++r) {
+                            while (__any_sync(0xffffffffu, rem[r] != 0u)) {
+                                const int t = 4 * r + g;
+                                const int hd = rem[r] ? __ffs(rem[r]) - 1 : 0;
+                                const float v = canon_row_dot<T, HALVES>(kb, a.half_bytes, t,
+                                                                         qh0 + (int64_t)hd * a.q_stride_h,
+                                                                         j, a.scale_r);
+                                if (rem[r]) keyr[r] = max(keyr[r], ordered_key(v));
+                                rem[r] &= rem[r] - 1u;
+                            }
+                        }
+                        if (j == 0) {
+#pragma unroll
+                            for (int r = 0; r < 4; ++r) sm.red[slot][warp][4 * r + g] = keyr[r];
+                        }
+                        __syncwarp();   // orders the lanes' key stores before lane 0's release
+                        if (lane == 0) mbar_arrive(&sm.scored[slot]);
+                    }
+                }
+
                 // ---- 1. scores, canonical order (MODE 0: also the logits) ----------------
                 float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                if constexpr (MODE != 1) {
+                if constexpr (MODE != 1 && !SCREEN) {
 #pragma unroll
                 for (int r = 0; r < 4; ++r) {
                     const int t = 4 * r + g;
@@ -555,7 +719,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                 // ---- 2. resonance: max over this warp's heads --------------------------
                 // The fold over kv heads, the EWMA and the store are the salience
                 // finisher's; this warp stores one key per token and arrives on scored.
-                if (MODE != 1 && a.score) {
+                if (MODE != 1 && !SCREEN && a.score) {
                     // transpose-max over the 8 lanes of the group: afterwards lane j holds
                     // the max over heads of round rj = 2*bit2(j) + bit1(j), i.e. token 4*rj + g
                     uint32_t key[4];
@@ -589,7 +753,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                 // ---- 3. online softmax + P.V on tensor cores ------------------------------
                 if (a.attend) {
                     bool any_raise = false;
-                    if constexpr (MODE == 0) {
+                    if constexpr (MODE == 0 && !SCREEN) {
                         float z[4];
                         float mx = -INFINITY;
 #pragma unroll
@@ -627,16 +791,19 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                         // fragments straight from the swizzled K stage by ldmatrix.  Lane
                         // holds tokens tA = lane/4 and tA + 8 of heads nA = 2(lane%4), nA + 1
                         // -- the accumulator's own columns, so rescaling stays in the lane.
-                        float c4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                        const int mi = lane >> 3;
-                        const int tk = (lane & 7) + 8 * (mi & 1);
+                        // (Screened instances computed them with the screen's mma above.)
+                        if constexpr (!SCREEN) {
+                            const int mi = lane >> 3;
+                            const int tk = (lane & 7) + 8 * (mi & 1);
 #pragma unroll
-                        for (int kk = 0; kk < D / 16; ++kk) {
-                            const int c8 = (kk & 3) * 2 + (mi >> 1);
-                            uint32_t a0, a1, a2, a3;
-                            ldsm_x4(kb + (kk >> 2) * a.half_bytes + tk * 128 + ((c8 ^ (tk & 7)) << 4),
-                                    a0, a1, a2, a3);
-                            mma_16816<kBf16>(c4, a0, a1, a2, a3, qf[kk][0], qf[kk][1]);
+                            for (int kk = 0; kk < D / 16; ++kk) {
+                                const int c8 = (kk & 3) * 2 + (mi >> 1);
+                                uint32_t a0, a1, a2, a3;
+                                ldsm_x4(kb + (kk >> 2) * a.half_bytes + tk * 128 +
+                                            ((c8 ^ (tk & 7)) << 4),
+                                        a0, a1, a2, a3);
+                                mma_16816<kBf16>(c4, a0, a1, a2, a3, qf[kk][0], qf[kk][1]);
+                            }
                         }
                         const int tA = lane >> 2, tB = tA + 8;
                         const int nA = 2 * (lane & 3), nB = nA + 1;
@@ -687,7 +854,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                     }
                     __syncwarp();
                     const int n0 = 2 * (lane & 3);
-                    if (MODE == 0 && any_raise) {
+                    if (MODE == 0 && !SCREEN && any_raise) {
                         const float al0 = sm.alpha[warp][n0], al1 = sm.alpha[warp][n0 + 1];
 #pragma unroll
                         for (int mt = 0; mt < MT; ++mt) {
@@ -725,7 +892,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
             const int64_t cfirst = (b * a.n_tiles) / a.W;
             const int64_t pidx = (c - cfirst) * wph + s;
             float* part = a.partials + ((b * a.maxc * wph + pidx) * a.Hq) * (int64_t)RS;
-            if constexpr (MODE == 0) {
+            if constexpr (MODE == 0 && !SCREEN) {
                 float l_tot = l_run + __shfl_xor_sync(0xffffffffu, l_run, 8);
                 l_tot += __shfl_xor_sync(0xffffffffu, l_tot, 16);
                 if (head_writer && g == 0 && hl < G) {

@@ -196,3 +196,52 @@ def test_scored_matches_oracle(B, Hq, Hkv, D, N, dtype):
     assert np.array_equal(got_S.view(np.uint32), expect_S.view(np.uint32))
     ref = O.attention(q_attn.float().numpy(), K, V)
     np.testing.assert_allclose(out.float().cpu().numpy(), ref, atol=2e-2, rtol=1e-2)
+
+
+def _tied_queries(q, Hkv, kind, seed):
+    """Query heads of each kv group made (nearly) equal, so that several heads of a token
+    fall inside the tensor-core screen's error window and take the canonical recompute."""
+    B, Hq, _, D = q.shape
+    G = Hq // Hkv
+    g = torch.Generator().manual_seed(seed)
+    base = q.float().view(B, Hkv, G, 1, D)[:, :, :1].expand(B, Hkv, G, 1, D).clone()
+    if kind == "tied":          # identical heads: every head is a candidate
+        x = base
+    elif kind == "near":        # heads one bf16 step apart in a few dimensions
+        x = base.clone()
+        bump = (torch.rand(B, Hkv, G, 1, D, generator=g) < 0.03).float()
+        x = x + bump * x.abs().clamp(min=1e-2) * (2.0 ** -7)
+    else:                       # "scaled": heads differ by powers of two
+        x = base * (2.0 ** torch.arange(G, dtype=torch.float32)).view(1, 1, G, 1, 1)
+    return x.reshape(B, Hq, 1, D).to(q.dtype)
+
+
+@pytest.mark.parametrize("kind", ["tied", "near", "scaled"])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("B,Hq,Hkv,D,N", [(1, 28, 4, 128, 5003), (2, 64, 8, 128, 777),
+                                          (3, 6, 1, 128, 333), (2, 16, 2, 64, 700)])
+def test_screened_resonance_with_tied_heads(B, Hq, Hkv, D, N, dtype, kind):
+    """5-8 query heads per kv head: the resonance comes from a tensor-core screen plus the
+    canonical dot of the candidate heads; with (nearly) tied heads many tokens have several
+    candidates and the salience must still equal the canonical max bit for bit."""
+    kpool, vpool, spool, pt, q = _setup(B, Hq, Hkv, D, N, dtype, seed=B * 7 + N)
+    q = _tied_queries(q, Hkv, kind, seed=N)
+    kd, vd, sd, ptd, qd = (t.cuda() for t in (kpool, vpool, spool, pt, q))
+    out = torch.empty_like(qd)
+    lib = _lib.load()
+    lay = _layout(kd, vd, ptd, N)
+    qs = Query(qd.data_ptr(), dtype_code(dtype), Hq, 1, qd.stride(0), qd.stride(1), qd.stride(2))
+    os_ = Output(out.data_ptr(), dtype_code(dtype), 0, out.stride(0), out.stride(1), out.stride(2))
+    sal = Salience(sd.data_ptr(), sd.stride(1), sd.stride(0))
+    ws = Workspace.get(qd.device, lib.rkv_decode_fused_workspace_size(qs, lay))
+    assert lib.rkv_decode_fused(qs, lay, sal, 0.98, 1.0 - 0.98, 0.0, os_, ws.data_ptr(),
+                                ws.numel(), torch.cuda.current_stream().cuda_stream) == 0
+    torch.cuda.synchronize()
+    assert int(ws[:4].view(torch.int32)[0]) == 0
+    K = _logical(kpool, pt, N).float().numpy()
+    V = _logical(vpool, pt, N).float().numpy()
+    expect_S = O.ewma(_sal_logical(spool, pt, N).numpy(), O.resonance(q.float().numpy(), K, 2), 0.98)
+    got_S = _sal_logical(sd.cpu(), pt, N).numpy()
+    assert np.array_equal(got_S.view(np.uint32), expect_S.view(np.uint32))
+    ref = O.attention(q.float().numpy(), K, V)
+    np.testing.assert_allclose(out.float().cpu().numpy(), ref, atol=2e-2, rtol=1e-2)
