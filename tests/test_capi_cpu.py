@@ -74,3 +74,23 @@ def test_zeroed_structures_are_rejected_not_crashed():
     assert lib.rkv_decode_attention_workspace_size(q, lay) > 0
     o.out, o.dtype = 16, 2
     assert lib.rkv_decode_attention(q, lay, 0.0, 0, o, None, 0, None) == 1
+
+
+def test_integration_stub_matches_the_binding():
+    """The ctypes stub printed in INTEGRATION.md declares the same structures as the
+    package's binding (and include/razorkv_b200.h), so a maintainer who pastes it passes
+    correctly laid-out arguments."""
+    import ctypes
+    with open(os.path.join(ROOT, "INTEGRATION.md")) as f:
+        text = f.read()
+    blocks = [b for b in re.findall(r"```python\n(.*?)```", text, flags=re.S)
+              if "_paged_attention_cuda" in b]
+    assert len(blocks) == 1
+    src = blocks[0].replace('ctypes.CDLL("librazorkv_b200.so")', f'ctypes.CDLL({_lib.LIB_PATH!r})')
+    ns = {}
+    exec(compile(src, "INTEGRATION.md:stub", "exec"), ns)
+    for stub, ours in ((ns["_KV"], _lib.KVLayout), (ns["_Q"], _lib.Query), (ns["_O"], _lib.Output)):
+        assert [n for n, _ in stub._fields_] == [n for n, _ in ours._fields_]
+        assert ctypes.sizeof(stub) == ctypes.sizeof(ours)
+        for (n, _), (m, _) in zip(stub._fields_, ours._fields_):
+            assert getattr(stub, n).offset == getattr(ours, m).offset
