@@ -57,8 +57,9 @@ constexpr int kComputeRegs = 224;
 constexpr int kProducerRegs = 56;
 constexpr int kTileTokens = 16;
 constexpr int kMaxStages = 6;
-constexpr int kSmemBudget = 200 * 1024;   // stage ring; the rest holds barriers and scratch
+constexpr int kSmemBudget = 192 * 1024;   // stage ring (3 x 64 KB or 6 x 32 KB stages)
 constexpr float kRescaleLog2 = 8.0f;      // lazy softmax rescale threshold (log2 units)
+constexpr int kQRowPitch = 128;           // elements between the query rows staged in smem
 
 struct DevArgs {
     const void* q; int64_t q_stride_b, q_stride_h;
@@ -94,8 +95,13 @@ struct SmemTail {             // placed after the stage ring
     float alpha[kComputeWarps][8];
     alignas(16) float sal_old[kMaxStages][kComputeWarps][kTileTokens];   // bulk-copied salience rows
     float new_norm[kMaxStages][kComputeWarps][8];   // ||k_h|| of the appended token, per kv head
+    // screened instances: each compute warp's copy of its kv head's query rows (the scoring
+    // query, in its own 16-bit type), read by the canonical recompute of candidate heads
+    alignas(16) uint16_t qrow[kComputeWarps][8][kQRowPitch];
     int abort;
 };
+// ring + tail + alignment slack within the 227 KB a CTA may use
+static_assert(kSmemBudget + sizeof(SmemTail) + 1024 <= 227 * 1024, "shared memory over budget");
 
 template <typename T>
 __device__ __forceinline__ float to_f(T x);
@@ -214,31 +220,51 @@ __device__ __forceinline__ int head_of_lane(int j) {
 constexpr float kScreenTol = 6.103515625e-05f;   // 2^-14
 constexpr uint32_t kAbsMask2 = 0x7fff7fffu;       // clears the sign of both bf16/fp16 halves
 
-__device__ __forceinline__ uint4 ldg128(const void* p) {
-    return __ldg(reinterpret_cast<const uint4*>(p));
-}
-
-// Canonical-order dot of K row t of the staged page (128-byte swizzled halves at kb) with
-// fl(q_row * scale): lane j of each 8-lane group owns chunk j of every 64-element half; two
-// FMA chains (even / odd element positions) from +0.0f; xor-4/2/1 butterfly.  Every lane of
-// the group returns the same value.  q_row must be 16-byte aligned.
-template <typename T, int HALVES>
-__device__ __forceinline__ float canon_row_dot(uint32_t kb, int half_bytes, int t,
-                                               const T* q_row, int j, float scale) {
-    uint64_t kp[HALVES * 4], qp[HALVES * 4];
+// Canonical-order dots of four (K row, query head) pairs of the staged page, one per 8-lane
+// group (in round r, group g takes K row t[r] and query row hd[r]): lane j of each group owns
+// chunk j of every 64-element half of the K row (128-byte swizzled halves at kb) and of the
+// query row (rows of kQRowPitch 16-bit elements at qb, scaled to fl(q * scale) here, exactly
+// as the canonical order defines); two FMA chains (even / odd
+// element positions) from +0.0f; xor-4/2/1 butterfly.  All loads of the four rounds are
+// issued first and the four chains and butterflies are interleaved, so the rounds overlap.
+// Every lane of a group returns its round's value in v[r].
+template <typename T, int D>
+__device__ __forceinline__ void canon_dots4(uint32_t kb, int half_bytes, const int (&t)[4],
+                                            uint32_t qb, const int (&hd)[4], int j, float scale,
+                                            float (&v)[4]) {
+    constexpr int HALVES = D / 64;
+    uint4 kw[4][HALVES], qw[4][HALVES];
 #pragma unroll
-    for (int hf = 0; hf < HALVES; ++hf) {
-        unpack8_pairs<T>(lds128(kb + hf * half_bytes + t * 128 + ((j ^ (t & 7)) << 4)), kp + hf * 4);
-        float f[8];
-        unpack8<T>(ldg128(q_row + hf * 64 + 8 * j), f);
+    for (int r = 0; r < 4; ++r) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-            qp[hf * 4 + i] = pack2(__fmul_rn(f[2 * i], scale), __fmul_rn(f[2 * i + 1], scale));
+        for (int hf = 0; hf < HALVES; ++hf) {
+            kw[r][hf] = lds128(kb + hf * half_bytes + t[r] * 128 + ((j ^ (t[r] & 7)) << 4));
+            qw[r][hf] = lds128(qb + (uint32_t)((hd[r] * kQRowPitch + hf * 64 + 8 * j) * 2));
+        }
     }
-    uint64_t x = 0ull;   // (+0.0f, +0.0f)
+    float part[4];
 #pragma unroll
-    for (int e = 0; e < HALVES * 4; ++e) ffma2(x, qp[e], kp[e]);
-    return group8_sum(sum_pair(x));
+    for (int r = 0; r < 4; ++r) {
+        uint64_t x = 0ull;   // (+0.0f, +0.0f)
+#pragma unroll
+        for (int hf = 0; hf < HALVES; ++hf) {
+            uint64_t kp[4];
+            float f[8];
+            unpack8_pairs<T>(kw[r][hf], kp);
+            unpack8<T>(qw[r][hf], f);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                ffma2(x, pack2(__fmul_rn(f[2 * i], scale), __fmul_rn(f[2 * i + 1], scale)), kp[i]);
+        }
+        part[r] = sum_pair(x);
+    }
+#pragma unroll
+    for (int m = 4; m >= 1; m >>= 1) {
+#pragma unroll
+        for (int r = 0; r < 4; ++r) part[r] = __fadd_rn(part[r], __shfl_xor_sync(0xffffffffu, part[r], m));
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) v[r] = part[r];
 }
 
 // MODE 0: one query; its canonical-order scores give the resonance and the attention logits.
@@ -506,6 +532,16 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                 qa[kk][0] = f0 & kAbsMask2;
                 qa[kk][1] = f1 & kAbsMask2;
             }
+            // this warp's copy of the G scoring-query rows for the canonical recompute
+            // (16-byte rows; the host requires 16-byte aligned query rows for these instances)
+            __syncwarp();   // the previous segment's reads of the copy are done
+            const T* qg = static_cast<const T*>(a.q) + b * a.q_stride_b + (int64_t)(h * G) * a.q_stride_h;
+            for (int idx = lane; idx < G * (D / 8); idx += 32) {
+                const int i = idx / (D / 8), c8 = idx % (D / 8);
+                const uint4 w = *reinterpret_cast<const uint4*>(qg + (int64_t)i * a.q_stride_h + c8 * 8);
+                sts128(smem_u32(&sm.qrow[warp][i][c8 * 8]), w);
+            }
+            __syncwarp();
         }
         if constexpr (MODE != 1 && !SCREEN) {
             // fl(q * scale) for this lane's K elements: chunk j of every 64-element half
@@ -656,30 +692,31 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                         mA |= __shfl_xor_sync(0xffffffffu, mA, 2);
                         mB |= __shfl_xor_sync(0xffffffffu, mB, 2);
                         // canonical dots of the candidates: round r, group g takes token 4r + g
-                        // and its lowest candidate head; further candidates (rare) follow
-                        const T* qh0 = static_cast<const T*>(a.q) + b * a.q_stride_b +
-                                       (int64_t)(h * G) * a.q_stride_h;
+                        // and its lowest candidate head (the four rounds run together); further
+                        // candidates (rare) follow, four at a time
+                        const uint32_t qb = smem_u32(&sm.qrow[warp][0][0]);
                         uint32_t keyr[4], rem[4];
+                        int tr[4], hr[4];
+                        float vr[4];
 #pragma unroll
                         for (int r = 0; r < 4; ++r) {
-                            const int t = 4 * r + g;
-                            const uint32_t msk = __shfl_sync(0xffffffffu, r < 2 ? mA : mB, (t & 7) * 4);
-                            const int hd = msk ? __ffs(msk) - 1 : 0;
-                            const float v = canon_row_dot<T, HALVES>(kb, a.half_bytes, t,
-                                                                     qh0 + (int64_t)hd * a.q_stride_h,
-                                                                     j, a.scale_r);
-                            keyr[r] = msk ? ordered_key(v) : 0u;
-                            rem[r] = msk & (msk - 1);
+                            tr[r] = 4 * r + g;
+                            rem[r] = __shfl_sync(0xffffffffu, r < 2 ? mA : mB, (tr[r] & 7) * 4);
+                            hr[r] = rem[r] ? __ffs(rem[r]) - 1 : 0;
                         }
+                        canon_dots4<T, D>(kb, a.half_bytes, tr, qb, hr, j, a.scale_r, vr);
 #pragma unroll
                         for (int r = 0; r < 4; ++r) {
-                            while (__any_sync(0xffffffffu, rem[r] != 0u)) {
-                                const int t = 4 * r + g;
-                                const int hd = rem[r] ? __ffs(rem[r]) - 1 : 0;
-                                const float v = canon_row_dot<T, HALVES>(kb, a.half_bytes, t,
-                                                                         qh0 + (int64_t)hd * a.q_stride_h,
-                                                                         j, a.scale_r);
-                                if (rem[r]) keyr[r] = max(keyr[r], ordered_key(v));
+                            keyr[r] = rem[r] ? ordered_key(vr[r]) : 0u;
+                            rem[r] &= rem[r] - 1u;
+                        }
+                        while (__any_sync(0xffffffffu, (rem[0] | rem[1] | rem[2] | rem[3]) != 0u)) {
+#pragma unroll
+                            for (int r = 0; r < 4; ++r) hr[r] = rem[r] ? __ffs(rem[r]) - 1 : 0;
+                            canon_dots4<T, D>(kb, a.half_bytes, tr, qb, hr, j, a.scale_r, vr);
+#pragma unroll
+                            for (int r = 0; r < 4; ++r) {
+                                if (rem[r]) keyr[r] = max(keyr[r], ordered_key(vr[r]));
                                 rem[r] &= rem[r] - 1u;
                             }
                         }
