@@ -30,6 +30,10 @@
  *   rkv_release_pages         the storage release implied by razorkv/cache.py:356-358
  *   rkv_gather_tokens         materialises the contiguous key_cache/value_cache tensors of
  *                             razorkv/cache.py:89-91 from the paged layout
+ *   rkv_append_partial,       the same steps (razorkv/cache.py:239-287, 361-393) for a rank
+ *   rkv_score_partial,        that holds only some kv heads of a layer: each writes its share
+ *   rkv_append_decode_partial of the salience update to an exchange block, and
+ *   rkv_salience_apply        rkv_salience_apply finishes it after an all-reduce MAX
  */
 #ifndef RAZORKV_B200_H
 #define RAZORKV_B200_H
@@ -253,6 +257,63 @@ int rkv_compact_tokens(const rkv_kv_layout* kv, const rkv_salience* sal,
 /* free_stack[free_top + i] = pages[i], i < n. */
 int rkv_release_pages(const int64_t* pages, int64_t n, int64_t* free_stack, int64_t free_top,
                       void* stream);
+
+/* ---- KV-head sharding ---------------------------------------------------------------------
+ * When the kv heads of a layer are spread over the ranks of a head group, no rank can finish
+ * a token's salience alone: the resonance is a max over every query head and the initial
+ * salience a mean over every kv head (razorkv/cache.py:239-247, :274-287).  The partial calls
+ * write this rank's share into an exchange block instead of updating the salience; the caller
+ * takes the element-wise int32 MAX of the blocks over the head group (an all-reduce MAX:
+ * exact and independent of the order of the ranks) and rkv_salience_apply then updates the
+ * salience, bit for bit as one rank holding every head would.
+ *
+ * Exchange block: int32 x[b * stride_b + ...] per sequence b.  Entry t < num_tokens holds the
+ * signed key of token t's resonance over this rank's query heads; entry
+ * norm_off + i * num_kv_heads_total + h holds the signed key of ||k|| of global kv head h of
+ * the i-th token the call appends (INT32_MIN where this rank does not hold head h).  The
+ * signed key of an fp32 value is its order-preserving uint32 key with the top bit flipped, so
+ * int32 order is the fp32 order.  The layout's kv heads are global heads head0 ..
+ * head0 + kv->num_kv_heads - 1. */
+typedef struct rkv_exchange {
+    int32_t* x;
+    int64_t stride_b;
+    int64_t norm_off;
+    int32_t head0;
+    int32_t num_kv_heads_total;
+} rkv_exchange;
+
+/* rkv_append that leaves the salience alone and writes the new tokens' norms (salience_init
+ * == RKV_SAL_NORM) to the exchange block (razorkv/cache.py:239-247, 369-390, one rank's heads). */
+int rkv_append_partial(const rkv_kv_layout* kv, const void* k_new, const void* v_new,
+                       int64_t new_stride_b, int64_t new_stride_h, int64_t new_stride_t,
+                       int64_t n_new, int64_t pos, int64_t* page_table, const int64_t* free_stack,
+                       int64_t free_top, int salience_init, const rkv_exchange* xc, void* stream);
+
+/* The resonance keys of every token of kv over this rank's query heads (q holds the query
+ * heads of the layout's kv heads only), written to the exchange block
+ * (razorkv/cache.py:249-280, one rank's heads). */
+int rkv_score_partial(const rkv_query* q, const rkv_kv_layout* kv, const rkv_exchange* xc,
+                      void* stream);
+
+/* rkv_append_decode whose scoring is partial: the appended token's norms and every token's
+ * resonance key go to the exchange block (nothing is written to the salience); the attention
+ * output covers this rank's query heads.  Follow with the all-reduce MAX and
+ * rkv_salience_apply(score_tokens = num_tokens + 1, new_first = num_tokens, n_new = 1). */
+int rkv_append_decode_partial(const rkv_kv_layout* kv,
+                              const void* k_new, const void* v_new, int64_t new_stride_b,
+                              int64_t new_stride_h, int64_t* page_table,
+                              const int64_t* free_stack, int64_t free_top, int salience_init,
+                              const rkv_query* q, float scale, const rkv_output* out,
+                              const rkv_exchange* xc, void* workspace, size_t workspace_bytes,
+                              void* stream);
+
+/* The salience update from a reduced exchange block (razorkv/cache.py:282-287 with the
+ * initial salience of :239-247): tokens [new_first, new_first + n_new) start from their mean
+ * norm (salience_init == RKV_SAL_NORM, sequential fp32 sum over the kv heads then one
+ * division) or 1.0; tokens t < score_tokens take S = fl(fl(decay S) + fl(one_minus_decay R)). */
+int rkv_salience_apply(const rkv_kv_layout* kv, const rkv_salience* sal, const rkv_exchange* xc,
+                       int64_t score_tokens, int64_t new_first, int64_t n_new,
+                       int salience_init, float decay, float one_minus_decay, void* stream);
 
 /* dst[b, h, t, :] = row (b, h, t) of kv (K when which == 0, V when 1), t < num_tokens;
  * dst is contiguous [B, Hkv, num_tokens, D] of kv->dtype.  sal_dst (optional, [B, num_tokens])

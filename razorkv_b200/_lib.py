@@ -53,6 +53,11 @@ class Salience(ctypes.Structure):
     _fields_ = [("s", c_vp), ("stride_b", c_i64), ("stride_p", c_i64)]
 
 
+class Exchange(ctypes.Structure):
+    _fields_ = [("x", c_vp), ("stride_b", c_i64), ("norm_off", c_i64), ("head0", c_i32),
+                ("num_kv_heads_total", c_i32)]
+
+
 P = ctypes.POINTER
 
 # name -> (restype, argtypes); mirrors include/razorkv_b200.h
@@ -94,6 +99,15 @@ _SIGNATURES = {
     "rkv_release_pages": (ctypes.c_int, [c_vp, c_i64, c_vp, c_i64, c_vp]),
     "rkv_gather_tokens": (ctypes.c_int, [P(KVLayout), ctypes.c_int, c_vp, P(Salience), c_vp,
                                          c_vp]),
+    "rkv_append_partial": (ctypes.c_int, [P(KVLayout), c_vp, c_vp, c_i64, c_i64, c_i64, c_i64,
+                                          c_i64, c_vp, c_vp, c_i64, ctypes.c_int, P(Exchange),
+                                          c_vp]),
+    "rkv_score_partial": (ctypes.c_int, [P(Query), P(KVLayout), P(Exchange), c_vp]),
+    "rkv_append_decode_partial": (ctypes.c_int, [P(KVLayout), c_vp, c_vp, c_i64, c_i64, c_vp,
+                                                 c_vp, c_i64, ctypes.c_int, P(Query), c_f32,
+                                                 P(Output), P(Exchange), c_vp, c_sz, c_vp]),
+    "rkv_salience_apply": (ctypes.c_int, [P(KVLayout), P(Salience), P(Exchange), c_i64, c_i64,
+                                          c_i64, ctypes.c_int, c_f32, c_f32, c_vp]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

@@ -36,7 +36,8 @@ from typing import Any, Callable, Dict, List, Optional, Tuple, Union
 import torch
 
 from . import _lib
-from ._lib import KVLayout, Output, Query, Salience, check, dtype_code, require_cuda, stream_ptr
+from ._lib import (Exchange, KVLayout, Output, Query, Salience, check, dtype_code, require_cuda,
+                   stream_ptr)
 from .config import RazorConfig
 from .kernels import Workspace
 
@@ -180,6 +181,11 @@ class PagedRazorKVCache(BaseCacheClass):
         self._layers: List[RazorLayerState] = []
         # selection hooks / diagnostics
         self.score_reducer: Optional[Callable[[torch.Tensor], torch.Tensor]] = None
+        # KV-head sharding (razorkv_b200.distributed.HeadGroup): this cache holds only some kv
+        # heads; every salience update goes through an exchange block combined over the group
+        self.head_group = None
+        self._xbuf: Optional[torch.Tensor] = None
+        self._xpend = None   # (layer, block, Exchange, score_tokens, new_first, n_new)
         # with record_decisions set, every compaction appends a SelectionRecord (device
         # tensors, read when the caller syncs); kept_override(layer, index, kept, margin) may
         # return a replacement kept-page tensor (to follow an external decision trace)
@@ -396,10 +402,19 @@ class PagedRazorKVCache(BaseCacheClass):
         lay = self._layout(layer_idx, n0)
         sal = self._salience()
         init = _lib.SAL_NORM if self.config.salience_init == "norm" else _lib.SAL_UNIFORM
-        st = lib.rkv_append(lay, sal, k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1),
-                            k.stride(2), T, n0, self._pt[layer_idx].data_ptr(),
-                            self._free.data_ptr(), self._free_top, init, self._stream())
-        check(st, "rkv_append")
+        if self.head_group is not None:
+            if self._xpend is None:   # an append outside update(): no scoring follows
+                self._xbegin(layer_idx, score_tokens=0, new_first=n0, n_new=T)
+            st = lib.rkv_append_partial(lay, k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1),
+                                        k.stride(2), T, n0, self._pt[layer_idx].data_ptr(),
+                                        self._free.data_ptr(), self._free_top, init,
+                                        self._xpend[2], self._stream())
+            check(st, "rkv_append_partial")
+        else:
+            st = lib.rkv_append(lay, sal, k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1),
+                                k.stride(2), T, n0, self._pt[layer_idx].data_ptr(),
+                                self._free.data_ptr(), self._free_top, init, self._stream())
+            check(st, "rkv_append")
         self._free_top -= new_pages
         self._n[layer_idx] = n0 + T
 
@@ -424,8 +439,52 @@ class PagedRazorKVCache(BaseCacheClass):
             return
         self._score(q, layer_idx, self._n[layer_idx])
 
+    # ----------------------------------------------------------------- KV-head sharding
+    def _xbegin(self, layer_idx: int, score_tokens: int, new_first: int, n_new: int):
+        """Open the exchange block of one salience update of a head-sharded layer: the keys
+        of score_tokens tokens, then the kv-head norms of the n_new tokens from new_first."""
+        H = self.head_group.num_kv_heads_total
+        stride = score_tokens + n_new * H
+        need = max(1, self._B * stride)
+        if self._xbuf is None or self._xbuf.numel() < need:
+            old = 0 if self._xbuf is None else self._xbuf.numel()
+            self._xbuf = torch.empty(max(need, 2 * old), dtype=torch.int32, device=self._device)
+        x = self._xbuf[: self._B * stride].view(self._B, stride)
+        xc = Exchange(x.data_ptr(), stride, score_tokens, self.head_group.head0, H)
+        self._xpend = (layer_idx, x, xc, score_tokens, new_first, n_new)
+
+    def _settle(self):
+        """Combine the open exchange block over the head group (all-reduce MAX) and update
+        the salience from it."""
+        if self._xpend is None:
+            return
+        layer_idx, x, xc, score_tokens, new_first, n_new = self._xpend
+        self._xpend = None
+        if x.numel():
+            self.head_group.reduce(x)
+        init = _lib.SAL_NORM if self.config.salience_init == "norm" else _lib.SAL_UNIFORM
+        decay = self.config.salience_decay
+        st = _lib.load().rkv_salience_apply(self._layout(layer_idx), self._salience(), xc,
+                                            score_tokens, new_first, n_new, init, float(decay),
+                                            float(1.0 - decay), self._stream())
+        check(st, "rkv_salience_apply")
+
     def _score(self, q: torch.Tensor, layer_idx: int, n_tokens: int):
         lib = _lib.load()
+        if self.head_group is not None:
+            standalone = self._xpend is None
+            if standalone:
+                self._xbegin(layer_idx, score_tokens=n_tokens, new_first=n_tokens, n_new=0)
+            elif self._xpend[3] != n_tokens:
+                raise RuntimeError("head-sharded scoring: exchange opened for a different length")
+            st = lib.rkv_score_partial(Query(q.data_ptr(), dtype_code(q.dtype), q.shape[1],
+                                             q.shape[2], q.stride(0), q.stride(1), q.stride(2)),
+                                       self._layout(layer_idx, n_tokens), self._xpend[2],
+                                       self._stream())
+            check(st, "rkv_score_partial")
+            if standalone:
+                self._settle()
+            return
         decay = self.config.salience_decay
         st = lib.rkv_score(Query(q.data_ptr(), dtype_code(q.dtype), q.shape[1], q.shape[2],
                                  q.stride(0), q.stride(1), q.stride(2)),
@@ -545,12 +604,19 @@ class PagedRazorKVCache(BaseCacheClass):
         T = key_states.shape[-2]
         is_prefill = T > 1
         first = self._n[layer_idx] is None
+        scored = cache_kwargs is not None and "query_states" in cache_kwargs
+        if self.head_group is not None:
+            if self.return_handles:
+                raise NotImplementedError("KV-head sharding does not serve the HF engine path")
+            n0 = self._n[layer_idx] or 0
+            self._xbegin(layer_idx, score_tokens=n0 + T if scored else 0, new_first=n0, n_new=T)
         self._append(layer_idx, key_states, value_states)
         if layer_idx == 0:
             self._seen_tokens = T if first else self._seen_tokens + T
         self._sync_layer(layer_idx)
-        if cache_kwargs is not None and "query_states" in cache_kwargs:
+        if scored:
             self.update_salience_with_query(cache_kwargs["query_states"], layer_idx)
+        self._settle()
         cur = self._n[layer_idx]
         budget = self._budget(layer_idx)
         if is_prefill:
@@ -595,11 +661,20 @@ class PagedRazorKVCache(BaseCacheClass):
         if key_states.shape[-2] != 1:
             raise ValueError("decode_step takes exactly one new token")
         first = self._n[layer_idx] is None
+        sharded = self.head_group is not None
+        if sharded:
+            n0 = self._n[layer_idx] or 0
+            self._xbegin(layer_idx, score_tokens=n0 + 1, new_first=n0, n_new=1)
         self._append(layer_idx, key_states, value_states)
         if layer_idx == 0:
             self._seen_tokens = 1 if first else self._seen_tokens + 1
         self._sync_layer(layer_idx)
         q = query_states if query_states.stride(-1) == 1 else query_states.contiguous()
+        if sharded:
+            # head-sharded: the exchange-based salience update, then compaction (every rank
+            # holds the same salience, so every rank keeps the same pages), then attention
+            self.update_salience_with_query(q, layer_idx)
+            self._settle()
         B, Hq, _, D = q.shape
         if out is None:
             out = torch.empty(B, Hq, 1, D, dtype=q.dtype, device=q.device)
@@ -611,9 +686,11 @@ class PagedRazorKVCache(BaseCacheClass):
                      out.stride(2))
         scale = float(scaling) if scaling else 0.0
         obs = self.launch_observer
-        if cur > budget + self.config.page_size:
-            self.update_salience_with_query(q, layer_idx)
-            self._evict_layer(layer_idx, budget)
+        if sharded or cur > budget + self.config.page_size:
+            if not sharded:
+                self.update_salience_with_query(q, layer_idx)
+            if cur > budget + self.config.page_size:
+                self._evict_layer(layer_idx, budget)
             lay = self._layout(layer_idx)
             ws = Workspace.get(self._device, lib.rkv_decode_attention_workspace_size(qs, lay))
             if obs is not None:
@@ -692,19 +769,33 @@ class PagedRazorKVCache(BaseCacheClass):
         obs = self.launch_observer
         if obs is not None:
             obs.before(layer_idx, 2 * B * self._Hkv * cur * D * self._elt)
-        st = self._lib.rkv_append_decode(
-            lay, self._sal_struct, k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1),
-            pt.data_ptr(), self._free.data_ptr(), self._free_top, self._sal_init, qs,
-            decay, 1.0 - decay, float(scaling) if scaling else 0.0, os_, ws.data_ptr(), ws.numel(),
-            stream)
+        if self.head_group is not None:
+            # head-sharded: keys and norms to the exchange block, then the MAX over the group
+            # and the salience update (below, once the token count is advanced)
+            self._xbegin(layer_idx, score_tokens=cur, new_first=n0, n_new=1)
+            st = self._lib.rkv_append_decode_partial(
+                lay, k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1), pt.data_ptr(),
+                self._free.data_ptr(), self._free_top, self._sal_init, qs,
+                float(scaling) if scaling else 0.0, os_, self._xpend[2], ws.data_ptr(),
+                ws.numel(), stream)
+            what = "rkv_append_decode_partial"
+        else:
+            st = self._lib.rkv_append_decode(
+                lay, self._sal_struct, k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1),
+                pt.data_ptr(), self._free.data_ptr(), self._free_top, self._sal_init, qs,
+                decay, 1.0 - decay, float(scaling) if scaling else 0.0, os_, ws.data_ptr(),
+                ws.numel(), stream)
+            what = "rkv_append_decode"
         if obs is not None:
             obs.after()
-        check(st, "rkv_append_decode")
+        check(st, what)
         if new_page:
             self._free_top -= 1
         self._n[layer_idx] = cur
         self._seen_tokens = seen
         self._layers[layer_idx].cumulative_length = seen
+        if self.head_group is not None:
+            self._settle()
         return out
 
     def check_errors(self) -> None:

@@ -194,13 +194,16 @@ int rkv_page_salience_pool(const float* sal, int64_t batch, int64_t seq_len, int
                                  pool_type == RKV_POOL_MEAN, out, S(stream)));
 }
 
-int rkv_append(const rkv_kv_layout* kv, const rkv_salience* sal, const void* k_new,
-               const void* v_new, int64_t new_stride_b, int64_t new_stride_h,
-               int64_t new_stride_t, int64_t n_new, int64_t pos, int64_t* page_table,
-               const int64_t* free_stack, int64_t free_top, int salience_init, void* stream) {
+// rkv_append and rkv_append_partial: sal may be null only with an exchange block (xc.x).
+static int append_impl(const rkv_kv_layout* kv, const rkv_salience* sal, const void* k_new,
+                       const void* v_new, int64_t new_stride_b, int64_t new_stride_h,
+                       int64_t new_stride_t, int64_t n_new, int64_t pos, int64_t* page_table,
+                       const int64_t* free_stack, int64_t free_top, int salience_init,
+                       const Exchange& xc, void* stream) {
     int st = check_kv(kv, true);
     if (st) return st;
-    if (!sal || !sal->s || !k_new || !v_new || !page_table || !free_stack) return RKV_ERR_INVALID_ARGUMENT;
+    if ((!xc.x && (!sal || !sal->s)) || !k_new || !v_new || !page_table || !free_stack)
+        return RKV_ERR_INVALID_ARGUMENT;
     if (n_new < 0 || pos < 0 || free_top < 0 || kv->page_size < 1) return RKV_ERR_INVALID_ARGUMENT;
     const int64_t P = kv->page_size;
     const int64_t first_new = (pos + P - 1) / P;
@@ -212,12 +215,14 @@ int rkv_append(const rkv_kv_layout* kv, const rkv_salience* sal, const void* k_n
     p.D = kv->head_dim; p.Hkv = (int)kv->num_kv_heads; p.B = kv->batch;
     p.stride_b = kv->stride_b; p.stride_h = kv->stride_h; p.stride_p = kv->stride_p;
     p.stride_t = kv->stride_t; p.page_size = P;
-    p.sal = sal->s; p.sal_stride_b = sal->stride_b; p.sal_stride_p = sal->stride_p;
+    p.sal = sal ? sal->s : nullptr; p.sal_stride_b = sal ? sal->stride_b : 0;
+    p.sal_stride_p = sal ? sal->stride_p : 0;
     p.k_new = k_new; p.v_new = v_new;
     p.new_stride_b = new_stride_b; p.new_stride_h = new_stride_h; p.new_stride_t = new_stride_t;
     p.n_new = n_new; p.pos = pos;
     p.page_table = page_table; p.free_stack = free_stack; p.free_top = free_top;
     p.salience_init = salience_init;
+    p.xc = xc;
     {
         const int64_t eb = kv->dtype == RKV_F32 ? 4 : 2;
         const int64_t strides[7] = {new_stride_b, new_stride_h, new_stride_t, kv->stride_b,
@@ -231,15 +236,27 @@ int rkv_append(const rkv_kv_layout* kv, const rkv_salience* sal, const void* k_n
     return status_of(launch_append(p, S(stream)));
 }
 
-int rkv_score(const rkv_query* q, const rkv_kv_layout* kv, const rkv_salience* sal,
-              float decay, float one_minus_decay, int ewma, void* stream) {
+int rkv_append(const rkv_kv_layout* kv, const rkv_salience* sal, const void* k_new,
+               const void* v_new, int64_t new_stride_b, int64_t new_stride_h,
+               int64_t new_stride_t, int64_t n_new, int64_t pos, int64_t* page_table,
+               const int64_t* free_stack, int64_t free_top, int salience_init, void* stream) {
+    if (!sal || !sal->s) return RKV_ERR_INVALID_ARGUMENT;
+    return append_impl(kv, sal, k_new, v_new, new_stride_b, new_stride_h, new_stride_t, n_new,
+                       pos, page_table, free_stack, free_top, salience_init, Exchange{}, stream);
+}
+
+// rkv_score and rkv_score_partial: sal may be null only with an exchange block (xc.x).
+static int score_impl(const rkv_query* q, const rkv_kv_layout* kv, const rkv_salience* sal,
+                      float decay, float one_minus_decay, int ewma, const Exchange& xc,
+                      void* stream) {
     int st = check_kv(kv, false);
     if (st) return st;
     if ((st = check_q(q, kv))) return st;
-    if (!sal || !sal->s) return RKV_ERR_INVALID_ARGUMENT;
+    if (!xc.x && (!sal || !sal->s)) return RKV_ERR_INVALID_ARGUMENT;
     if (kv->batch == 0 || kv->num_tokens == 0) return RKV_OK;
-    if (ewma && fast_ok(q, kv, false)) {
-        FusedParams p = fused_params(q, kv, sal, decay, one_minus_decay, 0.f, nullptr);
+    if ((ewma || xc.x) && fast_ok(q, kv, false)) {
+        FusedParams p = fused_params(q, kv, xc.x ? nullptr : sal, decay, one_minus_decay, 0.f, nullptr);
+        p.xc = xc;
         return status_of(launch_fused(p, S(stream)));
     }
     ScoreParams p{};
@@ -251,10 +268,18 @@ int rkv_score(const rkv_query* q, const rkv_kv_layout* kv, const rkv_salience* s
     p.stride_b = kv->stride_b; p.stride_h = kv->stride_h; p.stride_p = kv->stride_p;
     p.stride_t = kv->stride_t; p.page_size = kv->page_size;
     p.page_table = kv->page_table; p.pt_stride_b = kv->pt_stride_b;
-    p.sal = sal->s; p.sal_stride_b = sal->stride_b; p.sal_stride_p = sal->stride_p;
+    p.sal = sal ? sal->s : nullptr; p.sal_stride_b = sal ? sal->stride_b : 0;
+    p.sal_stride_p = sal ? sal->stride_p : 0;
     p.scale_r = resonance_scale(kv->head_dim);
     p.decay = decay; p.one_minus_decay = one_minus_decay; p.ewma = ewma;
+    p.xc = xc;
     return status_of(launch_score(p, S(stream)));
+}
+
+int rkv_score(const rkv_query* q, const rkv_kv_layout* kv, const rkv_salience* sal,
+              float decay, float one_minus_decay, int ewma, void* stream) {
+    if (!sal || !sal->s) return RKV_ERR_INVALID_ARGUMENT;
+    return score_impl(q, kv, sal, decay, one_minus_decay, ewma, Exchange{}, stream);
 }
 
 size_t rkv_decode_fused_workspace_size(const rkv_query* q, const rkv_kv_layout* kv) {
@@ -351,6 +376,107 @@ int rkv_append_decode(const rkv_kv_layout* kv, const rkv_salience* sal, const vo
     if (st) return st;
     return rkv_decode_fused(q, &grown, sal, decay, one_minus_decay, scale, out, workspace,
                             workspace_bytes, stream);
+}
+
+// ---- KV-head sharding -----------------------------------------------------------------------
+static int exchange_status(const rkv_exchange* xc, const rkv_kv_layout* kv, int64_t need_cols) {
+    if (!xc || !xc->x || xc->stride_b < need_cols || xc->norm_off < 0) return RKV_ERR_INVALID_ARGUMENT;
+    if (xc->head0 < 0 || xc->num_kv_heads_total < 1 ||
+        xc->head0 + kv->num_kv_heads > xc->num_kv_heads_total)
+        return RKV_ERR_INVALID_ARGUMENT;
+    return RKV_OK;
+}
+
+static Exchange exchange_of(const rkv_exchange* xc) {
+    Exchange e{};
+    e.x = xc->x; e.stride_b = xc->stride_b; e.norm_off = xc->norm_off;
+    e.h0 = xc->head0; e.htot = xc->num_kv_heads_total;
+    return e;
+}
+
+int rkv_append_partial(const rkv_kv_layout* kv, const void* k_new, const void* v_new,
+                       int64_t new_stride_b, int64_t new_stride_h, int64_t new_stride_t,
+                       int64_t n_new, int64_t pos, int64_t* page_table, const int64_t* free_stack,
+                       int64_t free_top, int salience_init, const rkv_exchange* xc, void* stream) {
+    int st = check_kv(kv, true);
+    if (st) return st;
+    if (n_new < 0) return RKV_ERR_INVALID_ARGUMENT;
+    if ((st = exchange_status(xc, kv, xc ? xc->norm_off + n_new * xc->num_kv_heads_total : 0)))
+        return st;
+    return append_impl(kv, nullptr, k_new, v_new, new_stride_b, new_stride_h, new_stride_t,
+                       n_new, pos, page_table, free_stack, free_top, salience_init,
+                       exchange_of(xc), stream);
+}
+
+int rkv_score_partial(const rkv_query* q, const rkv_kv_layout* kv, const rkv_exchange* xc,
+                      void* stream) {
+    int st = check_kv(kv, false);
+    if (st) return st;
+    if ((st = check_q(q, kv))) return st;
+    if ((st = exchange_status(xc, kv, kv->num_tokens))) return st;
+    return score_impl(q, kv, nullptr, 0.f, 0.f, 1, exchange_of(xc), stream);
+}
+
+int rkv_append_decode_partial(const rkv_kv_layout* kv,
+                              const void* k_new, const void* v_new, int64_t new_stride_b,
+                              int64_t new_stride_h, int64_t* page_table,
+                              const int64_t* free_stack, int64_t free_top, int salience_init,
+                              const rkv_query* q, float scale, const rkv_output* out,
+                              const rkv_exchange* xc, void* workspace, size_t workspace_bytes,
+                              void* stream) {
+    if (!kv) return RKV_ERR_INVALID_ARGUMENT;
+    rkv_kv_layout grown = *kv;
+    grown.num_tokens = kv->num_tokens + 1;
+    int st = check_kv(&grown, true);
+    if (st) return st;
+    if ((st = check_q(q, &grown))) return st;
+    if ((st = exchange_status(xc, kv, grown.num_tokens))) return st;
+    if (xc->stride_b < xc->norm_off + xc->num_kv_heads_total) return RKV_ERR_INVALID_ARGUMENT;
+    if (!out || !out->out) return RKV_ERR_INVALID_ARGUMENT;
+    const bool rows_aligned = k_new && v_new && !(reinterpret_cast<uintptr_t>(k_new) & 15) &&
+                              !(reinterpret_cast<uintptr_t>(v_new) & 15) &&
+                              !((new_stride_b * 2) & 15) && !((new_stride_h * 2) & 15);
+    if (page_table && free_stack && grown.batch > 0 && grown.page_table == page_table &&
+        grown.pt_stride_b == 0 && rows_aligned && fast_ok(q, &grown, true) &&
+        (kv->num_tokens % kv->page_size != 0 || free_top >= 1)) {
+        if (workspace_bytes < rkv_decode_fused_workspace_size(q, &grown) || !workspace)
+            return RKV_ERR_WORKSPACE_TOO_SMALL;
+        FusedParams p = fused_params(q, &grown, nullptr, 0.f, 0.f, scale, out);
+        p.partials = ws_body(workspace); p.counters = ws_counters(workspace); p.err = ws_err(workspace);
+        p.k_new = k_new; p.v_new = v_new; p.new_stride_b = new_stride_b;
+        p.new_stride_h = new_stride_h; p.pt_w = page_table; p.free_stack = free_stack;
+        p.free_top = free_top; p.sal_init_norm = salience_init == RKV_SAL_NORM;
+        p.xc = exchange_of(xc);
+        return status_of(launch_fused(p, S(stream)));
+    }
+    // shapes outside the fused kernel: append, score, attend
+    if ((st = rkv_append_partial(kv, k_new, v_new, new_stride_b, new_stride_h, 0, 1,
+                                 kv->num_tokens, page_table, free_stack, free_top, salience_init,
+                                 xc, stream)))
+        return st;
+    if ((st = rkv_score_partial(q, &grown, xc, stream))) return st;
+    return rkv_decode_attention(q, &grown, scale, 0, out, workspace, workspace_bytes, stream);
+}
+
+int rkv_salience_apply(const rkv_kv_layout* kv, const rkv_salience* sal, const rkv_exchange* xc,
+                       int64_t score_tokens, int64_t new_first, int64_t n_new,
+                       int salience_init, float decay, float one_minus_decay, void* stream) {
+    if (!kv || !sal || !sal->s) return RKV_ERR_INVALID_ARGUMENT;
+    if (kv->batch < 0 || (kv->page_table && kv->page_size < 1)) return RKV_ERR_INVALID_ARGUMENT;
+    if (score_tokens < 0 || new_first < 0 || n_new < 0) return RKV_ERR_INVALID_ARGUMENT;
+    const int64_t end = score_tokens > new_first + n_new ? score_tokens : new_first + n_new;
+    if (end > kv->num_tokens) return RKV_ERR_INVALID_ARGUMENT;
+    if (!xc || !xc->x || xc->stride_b < score_tokens || xc->num_kv_heads_total < 1 ||
+        (salience_init == RKV_SAL_NORM && n_new > 0 &&
+         xc->stride_b < xc->norm_off + n_new * xc->num_kv_heads_total))
+        return RKV_ERR_INVALID_ARGUMENT;
+    ApplyParams p{};
+    p.sal = sal->s; p.sal_stride_b = sal->stride_b; p.sal_stride_p = sal->stride_p;
+    p.page_table = kv->page_table; p.page_size = kv->page_size; p.B = kv->batch;
+    p.xc = exchange_of(xc);
+    p.score_tokens = score_tokens; p.new_first = new_first; p.n_new = n_new;
+    p.norm_init = salience_init == RKV_SAL_NORM; p.decay = decay; p.one_minus_decay = one_minus_decay;
+    return status_of(launch_apply(p, S(stream)));
 }
 
 int rkv_page_scores(const rkv_kv_layout* kv, const rkv_salience* sal, int64_t first_token,

@@ -81,6 +81,7 @@ struct DevArgs {
     // tokens at or past score_n keep their salience (MODE 2 scores the tokens before it)
     const void* q2; int64_t q2_stride_b, q2_stride_h;
     float attn_log2; int64_t score_n;
+    Exchange xc;   // head-sharded scoring: keys and norms go here, the salience is left alone
 };
 
 struct SmemTail {             // placed after the stage ring
@@ -381,6 +382,27 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                             const int64_t nv = a.N - tile * kTileTokens;
                             const int phys = sm.phys[slot][s];
                             if (t >= nv || phys < 0) continue;
+                            if (a.xc.x) {
+                                // head-sharded: the signed key of this rank's heads and the
+                                // appended token's kv-head norms go to the exchange block; the
+                                // salience is updated after the MAX over the ranks
+                                const int64_t tt = tile * kTileTokens + t;
+                                int32_t* xr = a.xc.x + b * a.xc.stride_b;
+                                if (tt < a.score_n) {
+                                    uint32_t key = 0u;
+                                    for (int hh = 0; hh < Hkv; ++hh) key = max(key, sm.red[slot][s * Hkv + hh][t]);
+                                    xr[tt] = signed_key_of(key);
+                                }
+                                if (append && tile == new_tile && t == new_row) {
+                                    for (int hh = 0; hh < a.xc.htot; ++hh) {
+                                        const int lh = hh - a.xc.h0;
+                                        xr[a.xc.norm_off + hh] =
+                                            (lh >= 0 && lh < Hkv) ? signed_key_of(ordered_key(sm.new_norm[slot][s][lh]))
+                                                                  : INT32_MIN;
+                                    }
+                                }
+                                continue;
+                            }
                             if (tile * kTileTokens + t >= a.score_n) {
                                 // not scored this step; only a token appended here gets its
                                 // initial salience
@@ -1318,15 +1340,15 @@ static cudaError_t launch_t(const FusedParams& f, const Plan& pl, CUtensorMapDat
     a.sal = f.sal; a.sal_stride_b = f.sal_stride_b; a.sal_stride_p = f.sal_stride_p;
     a.scale_r = f.scale_r; a.logit_log2 = f.logit_mul * 1.4426950408889634f;
     a.decay = f.decay; a.omd = f.one_minus_decay;
-    a.attend = f.attend; a.score = f.sal != nullptr;
-    a.sal_bulk = f.sal && !(reinterpret_cast<uintptr_t>(f.sal) & 15) && !((f.sal_stride_b * 4) & 15) &&
-                 !((f.sal_stride_p * 4) & 15);
+    a.attend = f.attend; a.score = f.sal != nullptr || f.xc.x != nullptr;
+    a.sal_bulk = f.sal && !f.xc.x && !(reinterpret_cast<uintptr_t>(f.sal) & 15) &&
+                 !((f.sal_stride_b * 4) & 15) && !((f.sal_stride_p * 4) & 15);
     a.out = f.out; a.o_stride_b = f.o_stride_b; a.o_stride_h = f.o_stride_h;
     a.partials = f.partials; a.counters = f.counters; a.err = f.err;
     a.stages = pl.stages; a.stage_bytes = pl.stage_bytes; a.tile_bytes = pl.tile_bytes;
     a.kv_tile_bytes = pl.kv_tile_bytes; a.half_bytes = pl.half_bytes;
     for (int i = 0; i < 3; ++i) a.role[i] = role[i];
-    a.k_new = (f.k_new && f.sal && f.attend) ? f.k_new : nullptr;
+    a.k_new = (f.k_new && (f.sal || f.xc.x) && f.attend) ? f.k_new : nullptr;
     a.v_new = f.v_new; a.new_stride_b = f.new_stride_b; a.new_stride_h = f.new_stride_h;
     a.pt_w = f.pt_w; a.free_stack = f.free_stack; a.free_top = f.free_top;
     a.sal_init_norm = f.sal_init_norm;
@@ -1339,6 +1361,7 @@ static cudaError_t launch_t(const FusedParams& f, const Plan& pl, CUtensorMapDat
     a.q2_stride_h = two_q ? f.q2_stride_h : f.q_stride_h;
     a.attn_log2 = f.scale_r * f.logit_mul * 1.4426950408889634f;
     a.score_n = f.has_score_n ? f.score_n : f.N;
+    a.xc = f.xc;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -1412,7 +1435,8 @@ cudaError_t launch_fused(const FusedParams& p, cudaStream_t st) {
     if (pl.grid == 0) return cudaSuccess;
     // attention only: tensor-core logits; two queries: canonical scores of q + tensor-core
     // logits of q2; otherwise one query serves both (canonical scores)
-    const int mode = !p.sal ? 1 : (p.q2 && p.attend) ? 2 : 0;
+    const bool scoring = p.sal != nullptr || p.xc.x != nullptr;
+    const int mode = !scoring ? 1 : (p.q2 && p.attend) ? 2 : 0;
     if (mode == 1 && !p.attend) return cudaErrorInvalidValue;
     const bool bf = p.dtype == RKV_BF16;
     const auto dt = bf ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;

@@ -95,6 +95,10 @@ score_kernel(ScoreParams p) {
         for (int it = 0; it < kScoreTPG; ++it) {
             int64_t t = t0 + group + 32 * it;
             if (t >= p.N) break;
+            if (p.xc.x) {   // head-sharded: this rank's key; the salience waits for the MAX
+                p.xc.x[(int64_t)b * p.xc.stride_b + t] = signed_key_of(best[it]);
+                continue;
+            }
             float R = key_to_float(best[it]);
             float* sp = p.sal + (p.page_table ? tm.page_table[t / p.page_size] * p.sal_stride_p +
                                                     (int64_t)b * p.sal_stride_b + t % p.page_size
@@ -496,7 +500,17 @@ append_kernel(AppendParams p) {
         if (active && j == 0) nrm[li * hk + h] = __fsqrt_rn(ss);
     }
     __syncthreads();
-    if (active && h0 == 0 && j == 0) {
+    if (active && h0 == 0 && j == 0 && p.xc.x) {
+        // head-sharded: this item's kv-head norms at their global head positions (others
+        // absent); the initial salience is set by rkv_salience_apply after the MAX
+        if (p.salience_init == RKV_SAL_NORM) {
+            int32_t* xr = p.xc.x + b * p.xc.stride_b + p.xc.norm_off + i * p.xc.htot;
+            for (int hh = 0; hh < p.xc.htot; ++hh) {
+                const int lh = hh - p.xc.h0;
+                xr[hh] = (lh >= 0 && lh < hk) ? signed_key_of(ordered_key(nrm[li * hk + lh])) : INT32_MIN;
+            }
+        }
+    } else if (active && h0 == 0 && j == 0) {
         float s0 = 1.0f;
         if (p.salience_init == RKV_SAL_NORM) {
             float acc = 0.0f;
@@ -586,8 +600,52 @@ __global__ void gather_kernel(GatherParams p) {
 }
 
 // ------------------------------------------------------------------------------------------
+// Salience update of a head-sharded step (razorkv/cache.py:239-247 and :282-287 once the
+// ranks' partial results are combined): the exchange block holds, after the MAX over the
+// ranks of the head group, every token's resonance key (max over all query heads) and the
+// appended tokens' norms of every kv head.  New tokens start from the mean norm (sequential
+// fp32 sum over kv heads, one division) or 1.0; scored tokens take the EWMA.
+// ------------------------------------------------------------------------------------------
+__global__ void apply_kernel(ApplyParams p) {
+    const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int64_t b = blockIdx.y;
+    const int64_t end = max(p.score_tokens, p.new_first + p.n_new);
+    if (t >= end) return;
+    const int32_t* xr = p.xc.x + b * p.xc.stride_b;
+    float* sp = p.sal + (p.page_table ? p.page_table[t / p.page_size] * p.sal_stride_p +
+                                            b * p.sal_stride_b + t % p.page_size
+                                      : b * p.sal_stride_b + t);
+    const bool is_new = t >= p.new_first && t < p.new_first + p.n_new;
+    float old;
+    if (is_new) {
+        old = 1.0f;
+        if (p.norm_init) {
+            const int32_t* nr = xr + p.xc.norm_off + (t - p.new_first) * p.xc.htot;
+            float acc = 0.0f;
+            for (int h = 0; h < p.xc.htot; ++h) acc = __fadd_rn(acc, key_to_float(ordered_of(nr[h])));
+            old = __fdiv_rn(acc, (float)p.xc.htot);
+        }
+    } else {
+        old = *sp;
+    }
+    if (t < p.score_tokens) {
+        const float R = key_to_float(ordered_of(xr[t]));
+        *sp = __fadd_rn(__fmul_rn(p.decay, old), __fmul_rn(p.one_minus_decay, R));
+    } else if (is_new) {
+        *sp = old;
+    }
+}
+
+// ------------------------------------------------------------------------------------------
 // launchers
 // ------------------------------------------------------------------------------------------
+cudaError_t launch_apply(const ApplyParams& p, cudaStream_t st) {
+    const int64_t end = p.score_tokens > p.new_first + p.n_new ? p.score_tokens : p.new_first + p.n_new;
+    if (end <= 0 || p.B <= 0) return cudaSuccess;
+    dim3 grid((unsigned)((end + 255) / 256), (unsigned)p.B);
+    apply_kernel<<<grid, 256, 0, st>>>(p);
+    return counted(cudaGetLastError(), 1);
+}
 cudaError_t launch_score(const ScoreParams& p, cudaStream_t st) {
     ScoreParams q = p;
     const int rows = (q.Hq / q.Hkv) * q.QL;

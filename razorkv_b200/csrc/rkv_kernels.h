@@ -14,6 +14,22 @@ inline cudaError_t counted(cudaError_t e, int n) {
     return e;
 }
 
+// Exchange block of head-sharded scoring (see rkv_exchange in the public header): signed
+// keys x[b * stride_b + t] of the resonance, x[b * stride_b + norm_off + i * htot + h] of the
+// kv-head norms of the i-th appended token.  x == nullptr: the salience is updated in place.
+struct Exchange {
+    int32_t* x; int64_t stride_b, norm_off; int h0, htot;
+};
+
+// Signed key of an fp32 value: the order-preserving uint32 key with its top bit flipped, so
+// that int32 MAX (an all-reduce MAX over ranks) orders like the floats.  INT32_MIN = absent.
+__host__ __device__ inline int32_t signed_key_of(uint32_t ordered) {
+    return (int32_t)(ordered ^ 0x80000000u);
+}
+__host__ __device__ inline uint32_t ordered_of(int32_t signed_key) {
+    return (uint32_t)signed_key ^ 0x80000000u;
+}
+
 struct ScoreParams {
     const void* q; int q_dtype; int64_t q_stride_b, q_stride_h, q_stride_t;
     int Hq, QL;
@@ -23,6 +39,7 @@ struct ScoreParams {
     float* sal; int64_t sal_stride_b, sal_stride_p;
     float scale_r, decay, one_minus_decay; int ewma;
     int rows_per_chunk;
+    Exchange xc;   // x != nullptr: write keys, leave the salience
 };
 
 struct AttnParams {
@@ -52,6 +69,16 @@ struct AppendParams {
     int64_t* page_table; const int64_t* free_stack; int64_t free_top;
     int salience_init;
     int vec_ok;   // every row 16-byte aligned and D a whole number of 16-byte chunks
+    Exchange xc;  // x != nullptr: write the new tokens' kv-head norms, leave the salience
+};
+
+// rkv_salience_apply: the salience update of a head-sharded step from the reduced exchange.
+struct ApplyParams {
+    float* sal; int64_t sal_stride_b, sal_stride_p;
+    const int64_t* page_table; int64_t page_size; int64_t B;
+    Exchange xc;
+    int64_t score_tokens, new_first, n_new;
+    int norm_init; float decay, one_minus_decay;
 };
 
 struct CompactTokensParams {
@@ -89,6 +116,9 @@ struct FusedParams {
     const void* q2; int64_t q2_stride_b, q2_stride_h;
     // tokens at or past score_n keep their salience (has_score_n == 0: all are scored)
     int has_score_n; int64_t score_n;
+    // head-sharded (partial) scoring: instead of updating the salience, write the signed
+    // resonance keys of the local heads and the appended token's kv-head norms here
+    Exchange xc;
 };
 
 cudaError_t launch_score(const ScoreParams& p, cudaStream_t st);
@@ -109,6 +139,7 @@ cudaError_t launch_compact_tokens(const CompactTokensParams& p, cudaStream_t st)
 cudaError_t launch_release(const int64_t* pages, int64_t n, int64_t* free_stack, int64_t top,
                            cudaStream_t st);
 cudaError_t launch_gather(const GatherParams& p, cudaStream_t st);
+cudaError_t launch_apply(const ApplyParams& p, cudaStream_t st);
 
 // fast path: returns cudaErrorNotSupported when the shape is outside its coverage
 bool fused_supported(int dtype, int D, int Hkv, int Hq, int64_t page_size, int64_t stride_t,

@@ -1,12 +1,23 @@
-"""Batch sharding of the cache across ranks (one process per GPU).
+"""Sharding of the cache across ranks (one process per GPU): by sequence and by kv head.
 
-Each rank holds all kv heads of its own B_local sequences, so scoring and attention need no
-communication.  Page selection does: the reference averages page scores over the *whole*
-batch before its top-k (razorkv/cache.py:335-341).  To keep the kept-page set identical to a
-single process holding the global batch, every rank all-gathers its [B_local, pages] page
-scores in rank order (global batch order), and every rank then runs the same
-sequential-sum mean and top-k on the same data.  The exchange happens only on compaction
-steps (about 64 KB per rank per compacting layer).
+Batch sharding.  Each rank holds all kv heads of its own B_local sequences, so scoring and
+attention need no communication.  Page selection does: the reference averages page scores
+over the *whole* batch before its top-k (razorkv/cache.py:335-341).  To keep the kept-page set
+identical to a single process holding the global batch, every rank all-gathers its
+[B_local, pages] page scores in rank order (global batch order), and every rank then runs the
+same sequential-sum mean and top-k on the same data.  The exchange happens only on
+compaction steps (about 64 KB per rank per compacting layer).
+
+KV-head sharding.  Each rank holds kv heads [head0, head0 + Hkv_local) of every sequence
+(and their query heads), so attention is local but a token's salience is not: the resonance
+is a max over every query head (razorkv/cache.py:280) and the initial salience a mean of
+||k|| over every kv head (razorkv/cache.py:241-243).  Every scoring call therefore writes this
+rank's share as order-preserving int32 keys into an exchange block, the ranks of the head
+group take the element-wise MAX (an all-reduce MAX: exact, so the result does not depend on
+the order of the ranks), and the salience update runs on the combined block, bit for bit as
+one process holding every head.  The exchange is one all-reduce of B * (tokens + kv heads)
+int32 per scored layer step.  Every rank then holds the same salience and selects the same
+pages with no further collective.
 """
 
 from typing import Callable, Optional
@@ -33,3 +44,33 @@ def batch_sharded_score_reducer(group: Optional[dist.ProcessGroup] = None
         return torch.cat(parts, dim=0)
 
     return reduce
+
+
+class HeadGroup:
+    """This rank's place in a KV-head shard group: it holds global kv heads
+    [head0, head0 + num_kv_heads_local) of num_kv_heads_total.  Install it as
+    ``PagedRazorKVCache.head_group``; ``reduce`` combines an exchange block over the group."""
+
+    def __init__(self, head0: int, num_kv_heads_local: int, num_kv_heads_total: int,
+                 group: Optional[dist.ProcessGroup] = None):
+        if head0 < 0 or num_kv_heads_local < 1 or head0 + num_kv_heads_local > num_kv_heads_total:
+            raise ValueError("kv head range outside the layer's heads")
+        self.head0 = head0
+        self.num_kv_heads_local = num_kv_heads_local
+        self.num_kv_heads_total = num_kv_heads_total
+        self.group = group
+
+    def reduce(self, x: torch.Tensor) -> None:
+        """Element-wise MAX of the int32 exchange block over the ranks of the group, in place."""
+        dist.all_reduce(x, op=dist.ReduceOp.MAX, group=self.group)
+
+
+def kv_head_shard(num_kv_heads: int, group: Optional[dist.ProcessGroup] = None) -> HeadGroup:
+    """The HeadGroup of this rank when a layer's kv heads are split evenly over ``group``
+    (rank r holds heads [r * Hkv / world, (r + 1) * Hkv / world))."""
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    if num_kv_heads % world:
+        raise ValueError(f"{num_kv_heads} kv heads do not split over {world} ranks")
+    local = num_kv_heads // world
+    return HeadGroup(rank * local, local, num_kv_heads, group)
