@@ -19,6 +19,7 @@ CPU fallback.  All of them are also registered as ``torch.ops.razorkv.*`` custom
 """
 
 import math
+import threading
 from typing import Optional, Tuple
 
 import torch
@@ -46,6 +47,7 @@ class Workspace:
     _pool = {}
     # error flags of workspaces replaced by larger ones (read by the next check)
     _retired = {}
+    _lock = threading.Lock()
 
     @classmethod
     def get(cls, device: torch.device, nbytes: int) -> torch.Tensor:
@@ -53,12 +55,13 @@ class Workspace:
         buf = cls._pool.get(key)
         if buf is None or buf.numel() < nbytes:
             size = max(nbytes, 1 << 20)
-            if buf is not None:
-                size = max(size, 2 * buf.numel())
-                # keep the old flag word until it has been checked
-                cls._retired.setdefault(device.index, []).append(cls._flag(buf).clone())
-            buf = torch.zeros(size, dtype=torch.uint8, device=device)
-            cls._pool[key] = buf
+            with cls._lock:
+                if buf is not None:
+                    size = max(size, 2 * buf.numel())
+                    # keep the old flag word until it has been checked
+                    cls._retired.setdefault(device.index, []).append(cls._flag(buf).clone())
+                buf = torch.zeros(size, dtype=torch.uint8, device=device)
+                cls._pool[key] = buf
         return buf
 
     @staticmethod
@@ -78,21 +81,22 @@ class Workspace:
         (one device synchronisation), so call it at sync points -- after a generation, at the
         end of a timed region, in tests -- not inside the decode loop."""
         codes = []
-        for (dev, _), buf in list(cls._pool.items()):
-            if device is not None and dev != torch.device(device).index:
-                continue
-            flag = cls._flag(buf)
-            code = int(flag.item())
-            if code:
-                codes.append(code)
-                if clear:
-                    flag.zero_()
-        for dev in list(cls._retired):
-            if device is not None and dev != torch.device(device).index:
-                continue
-            codes += [int(f.item()) for f in cls._retired[dev] if int(f.item())]
-            if clear:
-                del cls._retired[dev]
+        want = None if device is None else torch.device(device).index
+        with cls._lock:
+            for (dev, _), buf in list(cls._pool.items()):
+                if want is not None and dev != want:
+                    continue
+                flag = cls._flag(buf)
+                code = int(flag.item())
+                if code:
+                    codes.append(code)
+                    if clear:
+                        flag.zero_()
+            for dev in list(cls._retired):
+                if want is not None and dev != want:
+                    continue
+                flags = cls._retired.pop(dev, []) if clear else cls._retired.get(dev, [])
+                codes += [int(f.item()) for f in flags if int(f.item())]
         if codes:
             raise _lib.DeviceError(max(codes))
 
