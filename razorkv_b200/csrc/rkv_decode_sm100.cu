@@ -96,13 +96,18 @@ struct SmemTail {             // placed after the stage ring
     float alpha[kComputeWarps][8];
     alignas(16) float sal_old[kMaxStages][kComputeWarps][kTileTokens];   // bulk-copied salience rows
     float new_norm[kMaxStages][kComputeWarps][8];   // ||k_h|| of the appended token, per kv head
-    // screened instances: each compute warp's copy of its kv head's query rows (the scoring
-    // query, in its own 16-bit type), read by the canonical recompute of candidate heads
-    alignas(16) uint16_t qrow[kComputeWarps][8][kQRowPitch];
     int abort;
 };
+
+// Screened instances only, after the tail: each compute warp's copy of its kv head's query
+// rows (the scoring query, in its own 16-bit type), read by the canonical recompute of
+// candidate heads.  The other instances do not allocate it.
+struct QRows {
+    alignas(16) uint16_t q[kComputeWarps][8][kQRowPitch];
+};
 // ring + tail + alignment slack within the 227 KB a CTA may use
-static_assert(kSmemBudget + sizeof(SmemTail) + 1024 <= 227 * 1024, "shared memory over budget");
+static_assert(kSmemBudget + sizeof(SmemTail) + sizeof(QRows) + 1024 <= 227 * 1024,
+              "shared memory over budget");
 
 template <typename T>
 __device__ __forceinline__ float to_f(T x);
@@ -273,6 +278,8 @@ __device__ __forceinline__ void canon_dots4(uint32_t kb, int half_bytes, const i
 // MODE 2: two queries: the canonical-order scores of q (resonance, tokens before score_n)
 //         and the mma.sync logits of q2 (attention over all tokens) -- the HF hook path,
 //         where the hook scores with the pre-RoPE query and attention uses the post-RoPE one.
+// MODE 3: MODE 0 for a rank holding some kv heads of the layer: the resonance keys and the
+//         appended token's kv-head norms go to the exchange block, the salience is untouched.
 template <typename T, int D, int GP, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
 decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
@@ -281,15 +288,20 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
     constexpr int EPL = D / 8;          // K elements a lane owns per row
     constexpr int MT = D / 16;          // 16-dim mma row tiles
     constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+    // MODE 3 is MODE 0 whose scoring is partial (head-sharded): the finisher writes the
+    // exchange block instead of the salience.  Everything else follows MODE 0.
+    constexpr bool XCH = MODE == 3;
+    constexpr int M = XCH ? 0 : MODE;
     // 5-8 query heads per kv head: resonance by the tensor-core screen (see kScreenTol) and
-    // attention logits on tensor cores, as in MODE 1
-    constexpr bool SCREEN = GP == 8 && MODE != 1;
+    // attention logits on tensor cores, as in M 1
+    constexpr bool SCREEN = GP == 8 && M != 1;
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
     const int NS = a.stages;
     SmemTail& sm = *reinterpret_cast<SmemTail*>(smem + NS * a.stage_bytes);
+    QRows& qrows = *reinterpret_cast<QRows*>(smem + NS * a.stage_bytes + sizeof(SmemTail));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -382,7 +394,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                             const int64_t nv = a.N - tile * kTileTokens;
                             const int phys = sm.phys[slot][s];
                             if (t >= nv || phys < 0) continue;
-                            if (a.xc.x) {
+                            if constexpr (XCH) {
                                 // head-sharded: the signed key of this rank's heads and the
                                 // appended token's kv-head norms go to the exchange block; the
                                 // salience is updated after the MAX over the ranks
@@ -526,11 +538,11 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
     const bool head_writer = (j & ((8 / GP) - 1)) == 0;   // one lane per head in each group
     const uint32_t ps_base = smem_u32(&sm.ps[warp][0][0]);
 
-    // MODE 0 / 2 without the screen: fl(q * scale) as (even, odd) element pairs
+    // M 0 / 2 without the screen: fl(q * scale) as (even, odd) element pairs
     uint64_t qreg[SCREEN ? 1 : GP][EPL / 2];
-    uint32_t qf[D / 16][2];       // MODE 1 / 2 and screened MODE 0: q2^T as mma B fragments
-    // screened MODE 2: the score query's fragments; screened modes: their magnitudes
-    uint32_t qsf[(SCREEN && MODE == 2) ? D / 16 : 1][2];
+    uint32_t qf[D / 16][2];       // M 1 / 2 and screened M 0: q2^T as mma B fragments
+    // screened M 2: the score query's fragments; screened modes: their magnitudes
+    uint32_t qsf[(SCREEN && M == 2) ? D / 16 : 1][2];
     uint32_t qa[SCREEN ? D / 16 : 1][2];
     float acc[MT][4];
     int slot = 0;
@@ -541,8 +553,8 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
         const int64_t tb0 = pos - b * a.n_tiles, tb1 = seg_end - b * a.n_tiles;
 
         if constexpr (SCREEN) {
-            // B fragments of the score query q (MODE 2) and of the magnitudes of whichever
-            // query scores (q in both modes: in MODE 0 the attention query is q itself)
+            // B fragments of the score query q (M 2) and of the magnitudes of whichever
+            // query scores (q in both modes: in M 0 the attention query is q itself)
             const int n = lane >> 2;
             const T* qr = static_cast<const T*>(a.q) + b * a.q_stride_b + (int64_t)(h * G + n) * a.q_stride_h;
 #pragma unroll
@@ -550,7 +562,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                 const int d0 = kk * 16 + 2 * (lane & 3);
                 const uint32_t f0 = n < G ? pack_elems<T>(qr[d0], qr[d0 + 1]) : 0u;
                 const uint32_t f1 = n < G ? pack_elems<T>(qr[d0 + 8], qr[d0 + 9]) : 0u;
-                if constexpr (MODE == 2) { qsf[kk][0] = f0; qsf[kk][1] = f1; }
+                if constexpr (M == 2) { qsf[kk][0] = f0; qsf[kk][1] = f1; }
                 qa[kk][0] = f0 & kAbsMask2;
                 qa[kk][1] = f1 & kAbsMask2;
             }
@@ -561,11 +573,11 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
             for (int idx = lane; idx < G * (D / 8); idx += 32) {
                 const int i = idx / (D / 8), c8 = idx % (D / 8);
                 const uint4 w = *reinterpret_cast<const uint4*>(qg + (int64_t)i * a.q_stride_h + c8 * 8);
-                sts128(smem_u32(&sm.qrow[warp][i][c8 * 8]), w);
+                sts128(smem_u32(&qrows.q[warp][i][c8 * 8]), w);
             }
             __syncwarp();
         }
-        if constexpr (MODE != 1 && !SCREEN) {
+        if constexpr (M != 1 && !SCREEN) {
             // fl(q * scale) for this lane's K elements: chunk j of every 64-element half
             const T* qb = static_cast<const T*>(a.q) + b * a.q_stride_b;
 #pragma unroll
@@ -580,9 +592,9 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                 }
             }
         }
-        if constexpr (MODE != 0 || SCREEN) {
+        if constexpr (M != 0 || SCREEN) {
             // B = q2^T (dims x heads): lane holds head lane/4, dims 16kk + 2(lane%4) + {0,1}
-            // (b0) and the same + 8 (b1); heads past G are zero.  (q2 is q in MODE 0.)
+            // (b0) and the same + 8 (b1); heads past G are zero.  (q2 is q in M 0.)
             const int n = lane >> 2;
             const T* qr = static_cast<const T*>(a.q2) + b * a.q2_stride_b + (int64_t)(h * G + n) * a.q2_stride_h;
 #pragma unroll
@@ -592,8 +604,8 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                 qf[kk][1] = n < G ? pack_elems<T>(qr[d0 + 8], qr[d0 + 9]) : 0u;
             }
         }
-        float m_run = -INFINITY, l_run = 0.0f;   // MODE 0: running max / sum of head hl
-        // MODE 1 / 2: the same for heads nA = 2(lane % 4) and nB = nA + 1 (the accumulator's
+        float m_run = -INFINITY, l_run = 0.0f;   // M 0: running max / sum of head hl
+        // M 1 / 2: the same for heads nA = 2(lane % 4) and nB = nA + 1 (the accumulator's
         // columns of this lane)
         float mrA = -INFINITY, mrB = -INFINITY, lrA = 0.0f, lrB = 0.0f;
 #pragma unroll
@@ -651,8 +663,8 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                     if (lane == 0) sm.new_norm[slot][s][h] = nrm;
                 }
 
-                // attention logits in the mma accumulator layout (MODE 1 / 2 and screened
-                // MODE 0): tokens lane/4 and lane/4 + 8, heads 2(lane%4) and 2(lane%4) + 1
+                // attention logits in the mma accumulator layout (M 1 / 2 and screened
+                // M 0): tokens lane/4 and lane/4 + 8, heads 2(lane%4) and 2(lane%4) + 1
                 float c4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 
                 // ---- 1s. screened resonance (5-8 query heads per kv head) -----------------
@@ -668,7 +680,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                             uint32_t a0, a1, a2, a3;
                             ldsm_x4(kb + (kk >> 2) * a.half_bytes + tk * 128 + ((c8 ^ (tk & 7)) << 4),
                                     a0, a1, a2, a3);
-                            if constexpr (MODE == 2) {
+                            if constexpr (M == 2) {
                                 mma_16816<kBf16>(cs, a0, a1, a2, a3, qsf[kk][0], qsf[kk][1]);
                                 if (a.attend) mma_16816<kBf16>(c4, a0, a1, a2, a3, qf[kk][0], qf[kk][1]);
                             } else {
@@ -678,7 +690,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                                              a3 & kAbsMask2, qa[kk][0], qa[kk][1]);
                         }
                     }
-                    if constexpr (MODE == 0) {
+                    if constexpr (M == 0) {
 #pragma unroll
                         for (int e = 0; e < 4; ++e) c4[e] = cs[e];
                     }
@@ -716,7 +728,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                         // canonical dots of the candidates: round r, group g takes token 4r + g
                         // and its lowest candidate head (the four rounds run together); further
                         // candidates (rare) follow, four at a time
-                        const uint32_t qb = smem_u32(&sm.qrow[warp][0][0]);
+                        const uint32_t qb = smem_u32(&qrows.q[warp][0][0]);
                         uint32_t keyr[4], rem[4];
                         int tr[4], hr[4];
                         float vr[4];
@@ -751,9 +763,9 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                     }
                 }
 
-                // ---- 1. scores, canonical order (MODE 0: also the logits) ----------------
+                // ---- 1. scores, canonical order (M 0: also the logits) ----------------
                 float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                if constexpr (MODE != 1 && !SCREEN) {
+                if constexpr (M != 1 && !SCREEN) {
 #pragma unroll
                 for (int r = 0; r < 4; ++r) {
                     const int t = 4 * r + g;
@@ -778,7 +790,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                 // ---- 2. resonance: max over this warp's heads --------------------------
                 // The fold over kv heads, the EWMA and the store are the salience
                 // finisher's; this warp stores one key per token and arrives on scored.
-                if (MODE != 1 && !SCREEN && a.score) {
+                if (M != 1 && !SCREEN && a.score) {
                     // transpose-max over the 8 lanes of the group: afterwards lane j holds
                     // the max over heads of round rj = 2*bit2(j) + bit1(j), i.e. token 4*rj + g
                     uint32_t key[4];
@@ -812,7 +824,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                 // ---- 3. online softmax + P.V on tensor cores ------------------------------
                 if (a.attend) {
                     bool any_raise = false;
-                    if constexpr (MODE == 0 && !SCREEN) {
+                    if constexpr (M == 0 && !SCREEN) {
                         float z[4];
                         float mx = -INFINITY;
 #pragma unroll
@@ -913,7 +925,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                     }
                     __syncwarp();
                     const int n0 = 2 * (lane & 3);
-                    if (MODE == 0 && !SCREEN && any_raise) {
+                    if (M == 0 && !SCREEN && any_raise) {
                         const float al0 = sm.alpha[warp][n0], al1 = sm.alpha[warp][n0 + 1];
 #pragma unroll
                         for (int mt = 0; mt < MT; ++mt) {
@@ -951,7 +963,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
             const int64_t cfirst = (b * a.n_tiles) / a.W;
             const int64_t pidx = (c - cfirst) * wph + s;
             float* part = a.partials + ((b * a.maxc * wph + pidx) * a.Hq) * (int64_t)RS;
-            if constexpr (MODE == 0 && !SCREEN) {
+            if constexpr (M == 0 && !SCREEN) {
                 float l_tot = l_run + __shfl_xor_sync(0xffffffffu, l_run, 8);
                 l_tot += __shfl_xor_sync(0xffffffffu, l_tot, 16);
                 if (head_writer && g == 0 && hl < G) {
@@ -1327,7 +1339,7 @@ static cudaError_t launch_t(const FusedParams& f, const Plan& pl, CUtensorMapDat
         if (dev < 0 || dev >= 64 || !done[dev]) {
             const cudaError_t e = cudaFuncSetAttribute(
                 kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                kSmemBudget + (int)sizeof(SmemTail) + 1024);
+                kSmemBudget + (int)sizeof(SmemTail) + (int)sizeof(QRows) + 1024);
             if (e != cudaSuccess) return e;
             if (dev >= 0 && dev < 64) done[dev] = true;
         }
@@ -1365,10 +1377,11 @@ static cudaError_t launch_t(const FusedParams& f, const Plan& pl, CUtensorMapDat
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
+    constexpr bool kScreen = GP == 8 && MODE != 1;   // as SCREEN in decode_kernel
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)pl.grid);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = (size_t)pl.smem_bytes;
+    cfg.dynamicSmemBytes = (size_t)pl.smem_bytes + (kScreen ? sizeof(QRows) : 0);
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
@@ -1436,8 +1449,9 @@ cudaError_t launch_fused(const FusedParams& p, cudaStream_t st) {
     // attention only: tensor-core logits; two queries: canonical scores of q + tensor-core
     // logits of q2; otherwise one query serves both (canonical scores)
     const bool scoring = p.sal != nullptr || p.xc.x != nullptr;
-    const int mode = !scoring ? 1 : (p.q2 && p.attend) ? 2 : 0;
+    const int mode = !scoring ? 1 : (p.q2 && p.attend) ? 2 : p.xc.x ? 3 : 0;
     if (mode == 1 && !p.attend) return cudaErrorInvalidValue;
+    if (p.q2 && p.xc.x) return cudaErrorNotSupported;   // partial scoring of the two-query step
     const bool bf = p.dtype == RKV_BF16;
     const auto dt = bf ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const int gp = G <= 2 ? 2 : G <= 4 ? 4 : 8;
@@ -1447,6 +1461,9 @@ cudaError_t launch_fused(const FusedParams& p, cudaStream_t st) {
      : mode == 2 ? (gp == 2 ? launch_t<T_, D_, 2, 2>(p, pl, dt, st)                           \
                     : gp == 4 ? launch_t<T_, D_, 4, 2>(p, pl, dt, st)                         \
                               : launch_t<T_, D_, 8, 2>(p, pl, dt, st))                        \
+     : mode == 3 ? (gp == 2 ? launch_t<T_, D_, 2, 3>(p, pl, dt, st)                           \
+                    : gp == 4 ? launch_t<T_, D_, 4, 3>(p, pl, dt, st)                         \
+                              : launch_t<T_, D_, 8, 3>(p, pl, dt, st))                        \
                  : (gp == 2 ? launch_t<T_, D_, 2, 0>(p, pl, dt, st)                           \
                     : gp == 4 ? launch_t<T_, D_, 4, 0>(p, pl, dt, st)                         \
                               : launch_t<T_, D_, 8, 0>(p, pl, dt, st)))
