@@ -61,6 +61,10 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=0,
                     help="time K evenly spaced layers of the model only (for caches larger "
                          "than one GPU's memory); the JSON config records the subset")
+    ap.add_argument("--shard", default="auto", choices=["auto", "batch", "heads"],
+                    help="multi-GPU split: by sequence (weak scaling, batch per GPU fixed) or by "
+                         "kv head (strong scaling, one batch split over the GPUs' heads); auto "
+                         "splits heads when the batch is smaller than the GPU count")
     ap.add_argument("--event-every", type=int, default=8,
                     help="record per-launch CUDA events on every k-th timed step")
     return ap.parse_args()
@@ -347,14 +351,18 @@ def run_reference(args):
     return 0
 
 
-def workload_config(w, n):
+def workload_config(w, n, shard="batch"):
+    heads = shard == "heads" and n > 1
     return {
         "workload": w.name, "layers": w.num_layers, "q_heads": w.num_q_heads,
-        "kv_heads": w.num_kv_heads, "head_dim": w.head_dim, "batch_per_gpu": w.batch,
-        "global_batch": w.batch * n, "context": w.context, "page_size": w.page_size,
+        "kv_heads": w.num_kv_heads, "head_dim": w.head_dim,
+        "batch_per_gpu": w.batch, "global_batch": w.batch if heads else w.batch * n,
+        "kv_heads_per_gpu": w.num_kv_heads // n if heads else w.num_kv_heads,
+        "context": w.context, "page_size": w.page_size,
         "sink": w.sink_tokens, "window": w.local_window,
         "pyramid": f"{w.pyramid_mode} {w.pyramid_min_ratio}->{w.pyramid_max_ratio}",
-        "parallelism": f"batch-sharded x{n}" if n > 1 else "single GPU",
+        "parallelism": (f"kv-head-sharded x{n}" if heads else f"batch-sharded x{n}")
+                       if n > 1 else "single GPU",
         "l2": "inputs larger than L2 (retained KV per step >> 126 MB)",
     }
 
@@ -467,8 +475,23 @@ def main():
     w = WORKLOADS[args.workload]
     if args.context:
         w = w.scaled(context=args.context)
-    # each rank holds its own sequences (weak scaling): a distinct seed per rank
-    wr = w.scaled(seed=w.seed + 1000 * rank)
+    shard = args.shard
+    if shard == "auto":
+        shard = "heads" if (world > 1 and w.batch < world
+                            and w.num_kv_heads % world == 0) else "batch"
+    if world == 1:
+        shard = "none"
+    if shard == "heads":
+        # every rank decodes the same sequences with its own kv heads (strong scaling)
+        wr = w
+        h0 = rank * (w.num_kv_heads // world)
+        hkv = w.num_kv_heads // world
+    else:
+        # each rank holds its own sequences (weak scaling): a distinct seed per rank
+        wr = w.scaled(seed=w.seed + 1000 * rank)
+        h0, hkv = 0, w.num_kv_heads
+    G = w.group
+    kv_sl, q_sl = slice(h0, h0 + hkv), slice(h0 * G, (h0 + hkv) * G)
     cfg = w.razor_config()
     L, B = w.num_layers, w.batch
     if args.only_layer >= 0:
@@ -481,14 +504,22 @@ def main():
     total_steps = args.warmup + args.steps + args.e2e_steps
     cache = PagedRazorKVCache(cfg, L, max_slots=pool_slots(w, cfg, total_steps, layers))
 
-    if world > 1:
+    if shard == "batch":
         from razorkv_b200.distributed import batch_sharded_score_reducer
         cache.score_reducer = batch_sharded_score_reducer()
+    elif shard == "heads":
+        from razorkv_b200.distributed import kv_head_shard
+        cache.head_group = kv_head_shard(w.num_kv_heads)
+
+    def local(q, k, v):
+        """This rank's heads of one step's (or the prefill's) tensors."""
+        return (q[:, q_sl].contiguous(), k[:, kv_sl].contiguous(), v[:, kv_sl].contiguous())
 
     # ---- prefill (untimed)
     t0 = time.time()
     for l in layers:
         K, V, q0 = layer_prefill(wr, l, dev)
+        q0, K, V = local(q0, K, V)
         cache.update(K, V, l, {"query_states": q0})
         del K, V, q0
     torch.cuda.synchronize()
@@ -496,8 +527,9 @@ def main():
 
     # ---- decode inputs for every step, resident in HBM
     n_dev_steps = args.warmup + args.steps
-    inputs = [{l: decode_inputs(wr, s, l, dev) for l in layers} for s in range(n_dev_steps)]
-    outs = {l: torch.empty(B, w.num_q_heads, 1, w.head_dim, dtype=w.dtype, device=dev) for l in layers}
+    inputs = [{l: local(*decode_inputs(wr, s, l, dev)) for l in layers} for s in range(n_dev_steps)]
+    Hq_l = hkv * G
+    outs = {l: torch.empty(B, Hq_l, 1, w.head_dim, dtype=w.dtype, device=dev) for l in layers}
     timer = KernelTimer(torch, every=args.event_every)
     cache.launch_observer = timer
 
@@ -562,17 +594,21 @@ def main():
             }
         dist.barrier()
 
+    # sequences decoded by the whole job per step: every rank's own batch when sharding by
+    # sequence, one shared batch when sharding by kv head
+    seq_shards = 1 if shard == "heads" else world
+
     # ---- end to end: host inputs, public API, outputs back to the host
     e2e = None
     if args.e2e_steps > 0:
-        Hq, Hkv, D = w.num_q_heads, w.num_kv_heads, w.head_dim
+        Hq, Hkv, D = Hq_l, hkv, w.head_dim     # this rank's heads
         per_layer = B * (Hq + 2 * Hkv) * D
         host_in = []
         nl = len(layers)
         for s in range(n_dev_steps, total_steps):
             buf = torch.empty(nl, per_layer, dtype=w.dtype).pin_memory()
             for i, l in enumerate(layers):
-                q, k, v = decode_inputs(wr, s, l, "cpu")
+                q, k, v = local(*decode_inputs(wr, s, l, "cpu"))
                 buf[i] = torch.cat([q.reshape(-1), k.reshape(-1), v.reshape(-1)])
             host_in.append(buf)
         host_out = torch.empty(nl, B, Hq, 1, D, dtype=w.dtype).pin_memory()
@@ -631,7 +667,7 @@ def main():
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e_ms = float(t.item())
         elt = torch.tensor([], dtype=w.dtype).element_size()
-        e2e = {"value": world * B * args.e2e_steps / (e_ms / 1e3), "unit": "tokens/s",
+        e2e = {"value": seq_shards * B * args.e2e_steps / (e_ms / 1e3), "unit": "tokens/s",
                "steps": args.e2e_steps, "ms_per_step": e_ms / args.e2e_steps,
                "h2d_bytes_per_step": nl * per_layer * elt,
                "d2h_bytes_per_step": nl * B * Hq * D * elt,
@@ -650,7 +686,7 @@ def main():
     achieved = (kern_bytes / n_launch) / ((kern_ms / n_launch) / 1e3) / 1e9 if n_launch else 0.0
     tpb = traffic_per_byte()
     step_bytes = timer.all_bytes / max(args.steps, 1)
-    value = world * B * args.steps / (ms / 1e3)
+    value = seq_shards * B * args.steps / (ms / 1e3)
     line = {
         "metric": METRIC,
         "value": value,
@@ -660,11 +696,11 @@ def main():
         "warmup": args.warmup,
         "ms_per_step": ms / args.steps,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if shard == "heads" else "weak",
         "vs_baseline": None,
         "dtype": "bf16" if w.dtype == torch.bfloat16 else "fp32",
         "data": "synthetic: seeded N(0,1) K/V/q, 1% planted query-aligned pages per head",
-        "config": dict(workload_config(w, world), **({} if len(layers) == L else {
+        "config": dict(workload_config(w, world, shard), **({} if len(layers) == L else {
             "layer_subset": f"{len(layers)} of {L} layers ({layers[0]}..{layers[-1]}, evenly "
                             f"spaced); tokens/s counts the timed layers only"})),
         "impl": "b200",
