@@ -315,6 +315,30 @@ def oracle_sample(w, steps, warmup=0, threads=None, parity_dev=None):
     return res
 
 
+def reference_calibration(workload_name):
+    """The reference's own CPU path timed beside the oracle port on one host
+    (tests/golden/time_reference.py; the reference cannot travel to this host).  Returns the
+    record for the workload, or None."""
+    path = os.path.join(ROOT, "tests", "golden", "reference_timing.json")
+    try:
+        with open(path) as f:
+            rec = json.load(f)
+    except OSError:
+        return None
+    wl = rec.get("workloads", {}).get(workload_name)
+    if not wl:
+        return None
+    return {
+        "what": "the unmodified reference torch path (RazorKVCache.update + compacted_paged_sdpa) "
+                "and the oracle port timed on the same sample and the same host",
+        "host_cores": rec.get("cores"), "torch": rec.get("torch"),
+        "reference_torch_tokens_per_s": wl["reference_torch"]["tokens_per_s"],
+        "oracle_port_tokens_per_s": wl["oracle_port"]["tokens_per_s"],
+        "port_over_reference": wl["port_over_reference"],
+        "sample": wl["sample"],
+    }
+
+
 def run_reference(args):
     import torch
     from razorkv_b200.workload import WORKLOADS
@@ -343,7 +367,8 @@ def run_reference(args):
         "dtype": "bf16" if w.dtype == torch.bfloat16 else "fp32",
         "data": "synthetic: seeded N(0,1) K/V/q with planted query-aligned pages",
         "config": workload_config(w, args.gpus),
-        "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "cpu_baseline": dict({k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                             reference_torch_calibration=reference_calibration(w.name)),
         "e2e": {"value": res["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -736,6 +761,7 @@ def main():
             res = oracle_sample(w, steps=2, warmup=0, threads=os.cpu_count(), parity_dev=dev)
             line["cpu_baseline"] = {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")}
             line["cpu_baseline"]["ms_per_step_extrapolated"] = res["ms_per_step_est"]
+            line["cpu_baseline"]["reference_torch_calibration"] = reference_calibration(w.name)
             line["parity"] = res.get("parity")
         except Exception as exc:  # report, never hide
             line["cpu_baseline"] = {"error": repr(exc)}
