@@ -30,6 +30,10 @@
  *   rkv_release_pages         the storage release implied by razorkv/cache.py:356-358
  *   rkv_gather_tokens         materialises the contiguous key_cache/value_cache tensors of
  *                             razorkv/cache.py:89-91 from the paged layout
+ *   rkv_append_score_pool     razorkv/cache.py:361-393 and :322-331 (append, score, page
+ *                             max-pool of a compacting decode step, one pass over K)
+ *   rkv_select_compact_pages  razorkv/cache.py:333-359 (selection and pointer-only
+ *                             compaction in one launch)
  *   rkv_append_partial,       the same steps (razorkv/cache.py:239-287, 361-393) for a rank
  *   rkv_score_partial,        that holds only some kv heads of a layer: each writes its share
  *   rkv_append_decode_partial of the salience update to an exchange block, and
@@ -230,6 +234,29 @@ size_t rkv_select_pages_workspace_size(int64_t num_pages);
 int rkv_select_pages(const float* scores, int64_t batch, int64_t num_pages, int64_t k,
                      int64_t* kept, float* margin, void* workspace, size_t workspace_bytes,
                      void* stream);
+
+/* The score half of a compacting decode step in one pass over K (razorkv/cache.py:361-393
+ * and :322-331): append the new token (as rkv_append, position kv->num_tokens), score every
+ * token of the grown layer (as rkv_score, ewma = 1, q_len 1) and write the max-pooled page
+ * scores of the num_pages pages starting at token first_token to scores [B][num_pages]
+ * (as rkv_page_scores with sel_page_size = page_size).  The caller lowers its free-stack top
+ * by one when kv->num_tokens % page_size == 0. */
+int rkv_append_score_pool(const rkv_kv_layout* kv, const rkv_salience* sal, const void* k_new,
+                          const void* v_new, int64_t new_stride_b, int64_t new_stride_h,
+                          int64_t* page_table, const int64_t* free_stack, int64_t free_top,
+                          int salience_init, const rkv_query* q, float decay,
+                          float one_minus_decay, int64_t first_token, int64_t num_pages,
+                          float* scores, void* stream);
+
+/* rkv_select_pages followed by rkv_compact_pages in one launch (razorkv/cache.py:333-359):
+ * select the k pages with the largest batch mean of scores, then rewrite the shared page
+ * table and push the dropped pages (arguments as in the two calls; workspace as in
+ * rkv_select_pages).  kept[0..k) and margin receive the selection as rkv_select_pages. */
+int rkv_select_compact_pages(const float* scores, int64_t batch, int64_t num_pages, int64_t k,
+                             int64_t* page_table, int64_t sink_pages, int64_t tail_first_page,
+                             int64_t n_pages_total, int64_t* free_stack, int64_t free_top,
+                             int64_t* kept, float* margin, void* workspace,
+                             size_t workspace_bytes, void* stream);
 
 /* ---- cache: compaction -------------------------------------------------------------------
  * Pointer-only compaction of a shared page table whose haystack pages are

@@ -108,6 +108,12 @@ _SIGNATURES = {
                                                  P(Output), P(Exchange), c_vp, c_sz, c_vp]),
     "rkv_salience_apply": (ctypes.c_int, [P(KVLayout), P(Salience), P(Exchange), c_i64, c_i64,
                                           c_i64, ctypes.c_int, c_f32, c_f32, c_vp]),
+    "rkv_append_score_pool": (ctypes.c_int, [P(KVLayout), P(Salience), c_vp, c_vp, c_i64, c_i64,
+                                             c_vp, c_vp, c_i64, ctypes.c_int, P(Query), c_f32,
+                                             c_f32, c_i64, c_i64, c_vp, c_vp]),
+    "rkv_select_compact_pages": (ctypes.c_int, [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64,
+                                                c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_sz,
+                                                c_vp]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

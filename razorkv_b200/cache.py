@@ -655,6 +655,10 @@ class PagedRazorKVCache(BaseCacheClass):
                                       scaling)
         if fast is not None:
             return fast
+        fused = self._compact_step_fused(query_states, key_states, value_states, layer_idx, out,
+                                         scaling)
+        if fused is not None:
+            return fused
         self._ensure_layer(layer_idx)
         if self._k is None:
             self._init_pool(key_states)
@@ -711,6 +715,95 @@ class PagedRazorKVCache(BaseCacheClass):
             if obs is not None:
                 obs.after()
             check(st, "rkv_decode_fused")
+        return out
+
+    def _compact_step_fused(self, q, k, v, layer_idx, out, scaling):
+        """A compacting decode step with a page-aligned sink (razorkv/cache.py:361-414 then
+        the attention) in three launches: append + score + haystack page max-pool in one pass
+        over K (``rkv_append_score_pool``), selection + pointer-only compaction in one launch
+        (``rkv_select_compact_pages``), attention over the kept pages.  Returns None when the
+        step needs the general path (head sharding, a kept-set hook, an unaligned sink, the
+        no-haystack branch, or no compaction due)."""
+        if (self._k is None or layer_idx >= len(self._n) or self.head_group is not None
+                or self.kept_override is not None or self._pending):
+            return None
+        n0 = self._n[layer_idx]
+        if n0 is None or n0 == 0 or k.shape[2] != 1 or k.dtype != self._dtype:
+            return None
+        c = self.config
+        P = c.page_size
+        cur = n0 + 1
+        seen = self._seen_tokens + 1 if layer_idx == 0 else self._seen_tokens
+        num_layers = max(self.num_layers, len(self._n))
+        budget = c.get_layer_budget(layer_idx, num_layers, max(seen, cur))
+        if cur <= budget + P:
+            return None
+        sink = min(c.sink_tokens, cur)
+        local = min(c.local_window, cur - sink)
+        hs, he = sink, cur - local
+        hb = budget - sink - local
+        num_pages = (he - hs) // P if he > hs else 0
+        if hb <= 0 or num_pages <= 0 or hs % P:
+            return None
+        k_sel = max(1, min(num_pages, hb // P))
+        lib = _lib.load()
+        self._ensure_free(1)
+        self._ensure_pt(layer_idx, self._pages(cur))
+        q = q if q.stride(-1) == 1 else q.contiguous()
+        k = k if k.stride(-1) == 1 else k.contiguous()
+        v = v if v.stride(-1) == 1 else v.contiguous()
+        if k.stride() != v.stride():
+            k, v = k.contiguous(), v.contiguous()
+        B, Hq, _, D = q.shape
+        if out is None:
+            out = torch.empty(B, Hq, 1, D, dtype=q.dtype, device=q.device)
+        qs = Query(q.data_ptr(), dtype_code(q.dtype), Hq, 1, q.stride(0), q.stride(1), q.stride(2))
+        pt = self._pt[layer_idx]
+        stream = self._stream()
+        scores = torch.empty(self._B, num_pages, dtype=torch.float32, device=self._device)
+        decay = c.salience_decay
+        init = _lib.SAL_NORM if c.salience_init == "norm" else _lib.SAL_UNIFORM
+        st = lib.rkv_append_score_pool(self._layout(layer_idx, n0), self._salience(), k.data_ptr(),
+                                       v.data_ptr(), k.stride(0), k.stride(1), pt.data_ptr(),
+                                       self._free.data_ptr(), self._free_top, init, qs,
+                                       float(decay), float(1.0 - decay), hs, num_pages,
+                                       scores.data_ptr(), stream)
+        check(st, "rkv_append_score_pool")
+        if n0 % P == 0:
+            self._free_top -= 1
+        self._n[layer_idx] = cur
+        self._seen_tokens = seen
+        self._sync_layer(layer_idx)
+        if self.score_reducer is not None:
+            scores = self.score_reducer(scores).contiguous()
+        kept = torch.empty(k_sel, dtype=torch.int64, device=self._device)
+        margin = torch.empty(1, dtype=torch.float32, device=self._device)
+        ws = Workspace.get(self._device, lib.rkv_select_pages_workspace_size(num_pages))
+        sink_pages = hs // P
+        st = lib.rkv_select_compact_pages(scores.data_ptr(), scores.shape[0], num_pages, k_sel,
+                                          pt.data_ptr(), sink_pages, sink_pages + num_pages,
+                                          self._pages(cur), self._free.data_ptr(),
+                                          self._free_top, kept.data_ptr(), margin.data_ptr(),
+                                          ws.data_ptr(), ws.numel(), stream)
+        check(st, "rkv_select_compact_pages")
+        self._free_top += num_pages - k_sel
+        self._n[layer_idx] = sink + k_sel * P + (cur - (hs + num_pages * P))
+        self.compactions += 1
+        if self.record_decisions:
+            self.decisions.append(SelectionRecord(layer_idx, cur, budget, "pages", num_pages,
+                                                  k_sel, kept, margin))
+        os_ = Output(out.data_ptr(), dtype_code(out.dtype), 0, out.stride(0), out.stride(1),
+                     out.stride(2))
+        lay = self._layout(layer_idx)
+        ws = Workspace.get(self._device, lib.rkv_decode_attention_workspace_size(qs, lay))
+        obs = self.launch_observer
+        if obs is not None:
+            obs.before(layer_idx, self._kv_bytes(layer_idx))
+        st = lib.rkv_decode_attention(qs, lay, float(scaling) if scaling else 0.0, 0, os_,
+                                      ws.data_ptr(), ws.numel(), stream)
+        if obs is not None:
+            obs.after()
+        check(st, "rkv_decode_attention")
         return out
 
     def _decode_step_fast(self, q, k, v, layer_idx, out, scaling):

@@ -479,6 +479,63 @@ int rkv_salience_apply(const rkv_kv_layout* kv, const rkv_salience* sal, const r
     return status_of(launch_apply(p, S(stream)));
 }
 
+int rkv_append_score_pool(const rkv_kv_layout* kv, const rkv_salience* sal, const void* k_new,
+                          const void* v_new, int64_t new_stride_b, int64_t new_stride_h,
+                          int64_t* page_table, const int64_t* free_stack, int64_t free_top,
+                          int salience_init, const rkv_query* q, float decay,
+                          float one_minus_decay, int64_t first_token, int64_t num_pages,
+                          float* scores, void* stream) {
+    if (!kv || !sal || !sal->s || !scores) return RKV_ERR_INVALID_ARGUMENT;
+    rkv_kv_layout grown = *kv;
+    grown.num_tokens = kv->num_tokens + 1;
+    int st = check_kv(&grown, true);
+    if (st) return st;
+    if ((st = check_q(q, &grown))) return st;
+    if (first_token < 0 || num_pages < 0 || grown.page_size < 1 ||
+        first_token + num_pages * grown.page_size > grown.num_tokens)
+        return RKV_ERR_INVALID_ARGUMENT;
+    const bool rows_aligned = k_new && v_new && !(reinterpret_cast<uintptr_t>(k_new) & 15) &&
+                              !(reinterpret_cast<uintptr_t>(v_new) & 15) &&
+                              !((new_stride_b * 2) & 15) && !((new_stride_h * 2) & 15);
+    if (page_table && free_stack && grown.batch > 0 && grown.page_table == page_table &&
+        grown.pt_stride_b == 0 && rows_aligned && fast_ok(q, &grown, true) &&
+        first_token % grown.page_size == 0 &&
+        (kv->num_tokens % kv->page_size != 0 || free_top >= 1)) {
+        FusedParams p = fused_params(q, &grown, sal, decay, one_minus_decay, 0.f, nullptr);
+        p.k_new = k_new; p.v_new = v_new; p.new_stride_b = new_stride_b;
+        p.new_stride_h = new_stride_h; p.pt_w = page_table; p.free_stack = free_stack;
+        p.free_top = free_top; p.sal_init_norm = salience_init == RKV_SAL_NORM;
+        p.pool = scores; p.pool_first = first_token / grown.page_size; p.pool_num = num_pages;
+        return status_of(launch_fused(p, S(stream)));
+    }
+    // shapes outside the fused kernel: append, score, pool
+    if ((st = rkv_append(kv, sal, k_new, v_new, new_stride_b, new_stride_h, 0, 1, kv->num_tokens,
+                         page_table, free_stack, free_top, salience_init, stream)))
+        return st;
+    if ((st = rkv_score(q, &grown, sal, decay, one_minus_decay, 1, stream))) return st;
+    return num_pages ? rkv_page_scores(&grown, sal, first_token, num_pages, grown.page_size,
+                                       scores, stream)
+                     : RKV_OK;
+}
+
+int rkv_select_compact_pages(const float* scores, int64_t batch, int64_t num_pages, int64_t k,
+                             int64_t* page_table, int64_t sink_pages, int64_t tail_first_page,
+                             int64_t n_pages_total, int64_t* free_stack, int64_t free_top,
+                             int64_t* kept, float* margin, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+    if (!scores || !kept || !page_table || !free_stack || batch < 1 || num_pages < 1 || k < 1 ||
+        k > num_pages || sink_pages < 0 || free_top < 0)
+        return RKV_ERR_INVALID_ARGUMENT;
+    if (tail_first_page != sink_pages + num_pages || n_pages_total < tail_first_page)
+        return RKV_ERR_INVALID_ARGUMENT;
+    if (!workspace || workspace_bytes < rkv_select_pages_workspace_size(num_pages))
+        return RKV_ERR_WORKSPACE_TOO_SMALL;
+    return status_of(launch_select_compact(scores, batch, num_pages, k, kept, margin,
+                                           reinterpret_cast<uint32_t*>(ws_body(workspace)),
+                                           page_table, sink_pages, tail_first_page,
+                                           n_pages_total, free_stack, free_top, S(stream)));
+}
+
 int rkv_page_scores(const rkv_kv_layout* kv, const rkv_salience* sal, int64_t first_token,
                     int64_t num_pages, int64_t sel_page_size, float* scores, void* stream) {
     if (!kv || !sal || !sal->s || !scores) return RKV_ERR_INVALID_ARGUMENT;

@@ -82,6 +82,8 @@ struct DevArgs {
     const void* q2; int64_t q2_stride_b, q2_stride_h;
     float attn_log2; int64_t score_n;
     Exchange xc;   // head-sharded scoring: keys and norms go here, the salience is left alone
+    // MODE 4: page scores [B][pool_num] of logical pages pool_first .. pool_first + pool_num - 1
+    float* pool; int64_t pool_first, pool_num;
 };
 
 struct SmemTail {             // placed after the stage ring
@@ -291,9 +293,13 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
     // MODE 3 is MODE 0 whose scoring is partial (head-sharded): the finisher writes the
     // exchange block instead of the salience.  Everything else follows MODE 0.
     constexpr bool XCH = MODE == 3;
-    constexpr int M = XCH ? 0 : MODE;
+    // MODE 4 is MODE 0's score-only pass (no attention) of a compacting decode step: it also
+    // appends the new token and its finisher writes the max-pooled page scores of the
+    // haystack pages, so selection can follow at once.
+    constexpr bool POOL = MODE == 4;
+    constexpr int M = (XCH || POOL) ? 0 : MODE;
     // 5-8 query heads per kv head: resonance by the tensor-core screen (see kScreenTol) and
-    // attention logits on tensor cores, as in M 1
+    // attention logits on tensor cores, as in MODE 1
     constexpr bool SCREEN = GP == 8 && M != 1;
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -387,7 +393,49 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                 const int64_t tb0 = pos - b * a.n_tiles, tb1 = seg_end - b * a.n_tiles;
                 for (int64_t t0 = tb0; t0 < tb1; t0 += wph) {
                     const int ntile = (int)(tb1 - t0 < wph ? tb1 - t0 : wph);
-                    if (mbar_wait(&sm.scored[slot], par, a.err, &sm.abort)) {
+                    if constexpr (POOL) {
+                        // every lane takes part in every round (the page max is a shuffle
+                        // reduction over the 16 lanes of a tile)
+                        const bool ok = mbar_wait(&sm.scored[slot], par, a.err, &sm.abort);
+                        for (int i0 = 0; i0 < ntile * kTileTokens; i0 += 32) {
+                            const int i = i0 + lane;
+                            const bool in = ok && i < ntile * kTileTokens;
+                            const int s = in ? i / kTileTokens : 0, t = i % kTileTokens;
+                            const int64_t tile = t0 + s;
+                            const int64_t nv = a.N - tile * kTileTokens;
+                            const int phys = sm.phys[slot][s];
+                            uint32_t pk = 0u;   // ordered key of the token's new salience
+                            if (in && t < nv && phys >= 0) {
+                                uint32_t key = 0u;
+                                for (int hh = 0; hh < Hkv; ++hh) key = max(key, sm.red[slot][s * Hkv + hh][t]);
+                                const float R = key_to_float(key);
+                                float old;
+                                if (append && tile == new_tile && t == new_row) {
+                                    old = 1.0f;
+                                    if (a.sal_init_norm) {
+                                        float acc = 0.0f;
+                                        for (int hh = 0; hh < Hkv; ++hh)
+                                            acc = __fadd_rn(acc, sm.new_norm[slot][s][hh]);
+                                        old = __fdiv_rn(acc, (float)Hkv);
+                                    }
+                                } else {
+                                    old = a.sal_bulk ? sm.sal_old[slot][s][t]
+                                                     : a.sal[(int64_t)phys * a.sal_stride_p + b * a.sal_stride_b + t];
+                                }
+                                const float sn = __fadd_rn(__fmul_rn(a.decay, old), __fmul_rn(a.omd, R));
+                                a.sal[(int64_t)phys * a.sal_stride_p + b * a.sal_stride_b + t] = sn;
+                                pk = ordered_key(sn);
+                            }
+                            // page score = max over the tile's 16 tokens (NaN propagates, as
+                            // in torch.amax), for the haystack pages only
+#pragma unroll
+                            for (int o = 8; o >= 1; o >>= 1) pk = max(pk, __shfl_xor_sync(0xffffffffu, pk, o));
+                            if (in && t == 0) {
+                                const int64_t pg = tile - a.pool_first;
+                                if (pg >= 0 && pg < a.pool_num) a.pool[b * a.pool_num + pg] = key_to_float(pk);
+                            }
+                        }
+                    } else if (mbar_wait(&sm.scored[slot], par, a.err, &sm.abort)) {
                         for (int i = lane; i < ntile * kTileTokens; i += 32) {
                             const int s = i / kTileTokens, t = i % kTileTokens;
                             const int64_t tile = t0 + s;
@@ -538,10 +586,10 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
     const bool head_writer = (j & ((8 / GP) - 1)) == 0;   // one lane per head in each group
     const uint32_t ps_base = smem_u32(&sm.ps[warp][0][0]);
 
-    // M 0 / 2 without the screen: fl(q * scale) as (even, odd) element pairs
+    // MODE 0 / 2 without the screen: fl(q * scale) as (even, odd) element pairs
     uint64_t qreg[SCREEN ? 1 : GP][EPL / 2];
-    uint32_t qf[D / 16][2];       // M 1 / 2 and screened M 0: q2^T as mma B fragments
-    // screened M 2: the score query's fragments; screened modes: their magnitudes
+    uint32_t qf[D / 16][2];       // MODE 1 / 2 and screened MODE 0: q2^T as mma B fragments
+    // screened MODE 2: the score query's fragments; screened modes: their magnitudes
     uint32_t qsf[(SCREEN && M == 2) ? D / 16 : 1][2];
     uint32_t qa[SCREEN ? D / 16 : 1][2];
     float acc[MT][4];
@@ -553,8 +601,8 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
         const int64_t tb0 = pos - b * a.n_tiles, tb1 = seg_end - b * a.n_tiles;
 
         if constexpr (SCREEN) {
-            // B fragments of the score query q (M 2) and of the magnitudes of whichever
-            // query scores (q in both modes: in M 0 the attention query is q itself)
+            // B fragments of the score query q (MODE 2) and of the magnitudes of whichever
+            // query scores (q in both modes: in MODE 0 the attention query is q itself)
             const int n = lane >> 2;
             const T* qr = static_cast<const T*>(a.q) + b * a.q_stride_b + (int64_t)(h * G + n) * a.q_stride_h;
 #pragma unroll
@@ -594,7 +642,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
         }
         if constexpr (M != 0 || SCREEN) {
             // B = q2^T (dims x heads): lane holds head lane/4, dims 16kk + 2(lane%4) + {0,1}
-            // (b0) and the same + 8 (b1); heads past G are zero.  (q2 is q in M 0.)
+            // (b0) and the same + 8 (b1); heads past G are zero.  (q2 is q in MODE 0.)
             const int n = lane >> 2;
             const T* qr = static_cast<const T*>(a.q2) + b * a.q2_stride_b + (int64_t)(h * G + n) * a.q2_stride_h;
 #pragma unroll
@@ -604,8 +652,8 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                 qf[kk][1] = n < G ? pack_elems<T>(qr[d0 + 8], qr[d0 + 9]) : 0u;
             }
         }
-        float m_run = -INFINITY, l_run = 0.0f;   // M 0: running max / sum of head hl
-        // M 1 / 2: the same for heads nA = 2(lane % 4) and nB = nA + 1 (the accumulator's
+        float m_run = -INFINITY, l_run = 0.0f;   // MODE 0: running max / sum of head hl
+        // MODE 1 / 2: the same for heads nA = 2(lane % 4) and nB = nA + 1 (the accumulator's
         // columns of this lane)
         float mrA = -INFINITY, mrB = -INFINITY, lrA = 0.0f, lrB = 0.0f;
 #pragma unroll
@@ -637,9 +685,10 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                                        b * a.new_stride_b + (int64_t)h * a.new_stride_h + cidx * 8;
                         const uint4 w = *reinterpret_cast<const uint4*>(src);
                         const int hf = cidx >> 3, c8 = cidx & 7;
-                        sts128((isv ? vb : kb) + hf * a.half_bytes + new_row * 128 +
-                                   ((c8 ^ (new_row & 7)) << 4),
-                               w);
+                        if (!isv || a.attend)   // without attention no V is staged
+                            sts128((isv ? vb : kb) + hf * a.half_bytes + new_row * 128 +
+                                       ((c8 ^ (new_row & 7)) << 4),
+                                   w);
                         if (phys >= 0) {
                             T* dst = static_cast<T*>(isv ? a.vpool : a.kpool) + b * a.stride_b +
                                      (int64_t)h * a.stride_h + (int64_t)phys * a.stride_p +
@@ -663,8 +712,8 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                     if (lane == 0) sm.new_norm[slot][s][h] = nrm;
                 }
 
-                // attention logits in the mma accumulator layout (M 1 / 2 and screened
-                // M 0): tokens lane/4 and lane/4 + 8, heads 2(lane%4) and 2(lane%4) + 1
+                // attention logits in the mma accumulator layout (MODE 1 / 2 and screened
+                // MODE 0): tokens lane/4 and lane/4 + 8, heads 2(lane%4) and 2(lane%4) + 1
                 float c4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 
                 // ---- 1s. screened resonance (5-8 query heads per kv head) -----------------
@@ -763,7 +812,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                     }
                 }
 
-                // ---- 1. scores, canonical order (M 0: also the logits) ----------------
+                // ---- 1. scores, canonical order (MODE 0: also the logits) ----------------
                 float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
                 if constexpr (M != 1 && !SCREEN) {
 #pragma unroll
@@ -1360,7 +1409,7 @@ static cudaError_t launch_t(const FusedParams& f, const Plan& pl, CUtensorMapDat
     a.stages = pl.stages; a.stage_bytes = pl.stage_bytes; a.tile_bytes = pl.tile_bytes;
     a.kv_tile_bytes = pl.kv_tile_bytes; a.half_bytes = pl.half_bytes;
     for (int i = 0; i < 3; ++i) a.role[i] = role[i];
-    a.k_new = (f.k_new && (f.sal || f.xc.x) && f.attend) ? f.k_new : nullptr;
+    a.k_new = (f.k_new && (f.sal || f.xc.x) && (f.attend || f.pool)) ? f.k_new : nullptr;
     a.v_new = f.v_new; a.new_stride_b = f.new_stride_b; a.new_stride_h = f.new_stride_h;
     a.pt_w = f.pt_w; a.free_stack = f.free_stack; a.free_top = f.free_top;
     a.sal_init_norm = f.sal_init_norm;
@@ -1374,6 +1423,7 @@ static cudaError_t launch_t(const FusedParams& f, const Plan& pl, CUtensorMapDat
     a.attn_log2 = f.scale_r * f.logit_mul * 1.4426950408889634f;
     a.score_n = f.has_score_n ? f.score_n : f.N;
     a.xc = f.xc;
+    a.pool = f.pool; a.pool_first = f.pool_first; a.pool_num = f.pool_num;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -1449,9 +1499,11 @@ cudaError_t launch_fused(const FusedParams& p, cudaStream_t st) {
     // attention only: tensor-core logits; two queries: canonical scores of q + tensor-core
     // logits of q2; otherwise one query serves both (canonical scores)
     const bool scoring = p.sal != nullptr || p.xc.x != nullptr;
-    const int mode = !scoring ? 1 : (p.q2 && p.attend) ? 2 : p.xc.x ? 3 : 0;
+    const int mode = !scoring ? 1 : (p.q2 && p.attend) ? 2 : p.xc.x ? 3 : p.pool ? 4 : 0;
     if (mode == 1 && !p.attend) return cudaErrorInvalidValue;
     if (p.q2 && p.xc.x) return cudaErrorNotSupported;   // partial scoring of the two-query step
+    if (p.pool && (p.attend || p.xc.x || p.q2 || p.has_score_n || !p.sal))
+        return cudaErrorInvalidValue;                     // pooling is the score-only pass
     const bool bf = p.dtype == RKV_BF16;
     const auto dt = bf ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const int gp = G <= 2 ? 2 : G <= 4 ? 4 : 8;
@@ -1464,6 +1516,9 @@ cudaError_t launch_fused(const FusedParams& p, cudaStream_t st) {
      : mode == 3 ? (gp == 2 ? launch_t<T_, D_, 2, 3>(p, pl, dt, st)                           \
                     : gp == 4 ? launch_t<T_, D_, 4, 3>(p, pl, dt, st)                         \
                               : launch_t<T_, D_, 8, 3>(p, pl, dt, st))                        \
+     : mode == 4 ? (gp == 2 ? launch_t<T_, D_, 2, 4>(p, pl, dt, st)                           \
+                    : gp == 4 ? launch_t<T_, D_, 4, 4>(p, pl, dt, st)                         \
+                              : launch_t<T_, D_, 8, 4>(p, pl, dt, st))                        \
                  : (gp == 2 ? launch_t<T_, D_, 2, 0>(p, pl, dt, st)                           \
                     : gp == 4 ? launch_t<T_, D_, 4, 0>(p, pl, dt, st)                         \
                               : launch_t<T_, D_, 8, 0>(p, pl, dt, st)))

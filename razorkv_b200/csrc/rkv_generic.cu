@@ -318,9 +318,9 @@ __device__ __forceinline__ void select_digit(const int* hist, int rem, uint32_t 
     }
 }
 
-__global__ void __launch_bounds__(kSelThreads)
-select_kernel(const float* scores, int64_t B, int64_t n, int64_t k, int64_t* kept, float* margin,
-              uint32_t* gkeys) {
+// The selection of one CTA (select_kernel, select_compact_kernel).
+__device__ __forceinline__ void select_body(const float* scores, int64_t B, int64_t n, int64_t k,
+                                            int64_t* kept, float* margin, uint32_t* gkeys) {
     __shared__ int hist[256];
     __shared__ int warp_sums[32];
     __shared__ uint32_t s_prefix;
@@ -376,6 +376,12 @@ select_kernel(const float* scores, int64_t B, int64_t n, int64_t k, int64_t* kep
     }
 }
 
+__global__ void __launch_bounds__(kSelThreads)
+select_kernel(const float* scores, int64_t B, int64_t n, int64_t k, int64_t* kept, float* margin,
+              uint32_t* gkeys) {
+    select_body(scores, B, n, k, kept, margin, gkeys);
+}
+
 // ------------------------------------------------------------------------------------------
 // Pointer-only compaction (razorkv/cache.py:343-359 for a page-aligned sink).  One CTA.
 // ------------------------------------------------------------------------------------------
@@ -388,10 +394,10 @@ __device__ __forceinline__ int64_t lower_bound(const int64_t* a, int64_t n, int6
     return lo;
 }
 
-__global__ void __launch_bounds__(1024)
-compact_pages_kernel(int64_t* pt, int64_t sink_pages, int64_t num_pages, const int64_t* kept,
-                     int64_t k, int64_t tail_first, int64_t n_total, int64_t* free_stack,
-                     int64_t free_top) {
+__device__ __forceinline__ void compact_body(int64_t* pt, int64_t sink_pages, int64_t num_pages,
+                                             const int64_t* kept, int64_t k, int64_t tail_first,
+                                             int64_t n_total, int64_t* free_stack,
+                                             int64_t free_top) {
     // 1. push dropped haystack pages in ascending logical order
     for (int64_t j = threadIdx.x; j < num_pages; j += blockDim.x) {
         int64_t lb = lower_bound(kept, k, j);
@@ -410,6 +416,26 @@ compact_pages_kernel(int64_t* pt, int64_t sink_pages, int64_t num_pages, const i
         if (i < n_out) pt[sink_pages + i] = v;
         __syncthreads();
     }
+}
+
+__global__ void __launch_bounds__(1024)
+compact_pages_kernel(int64_t* pt, int64_t sink_pages, int64_t num_pages, const int64_t* kept,
+                     int64_t k, int64_t tail_first, int64_t n_total, int64_t* free_stack,
+                     int64_t free_top) {
+    compact_body(pt, sink_pages, num_pages, kept, k, tail_first, n_total, free_stack, free_top);
+}
+
+// Selection and pointer-only compaction in one launch (razorkv/cache.py:333-359): the CTA
+// selects, then -- after a barrier that makes its writes of the kept pages visible to every
+// thread of the CTA -- rewrites the page table and pushes the dropped pages.
+__global__ void __launch_bounds__(kSelThreads)
+select_compact_kernel(const float* scores, int64_t B, int64_t num_pages, int64_t k,
+                      int64_t* kept, float* margin, uint32_t* gkeys, int64_t* pt,
+                      int64_t sink_pages, int64_t tail_first, int64_t n_total,
+                      int64_t* free_stack, int64_t free_top) {
+    select_body(scores, B, num_pages, k, kept, margin, gkeys);
+    __syncthreads();
+    compact_body(pt, sink_pages, num_pages, kept, k, tail_first, n_total, free_stack, free_top);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -705,6 +731,16 @@ cudaError_t launch_page_scores(const PageScoreParams& p, cudaStream_t st) {
 cudaError_t launch_select(const float* scores, int64_t B, int64_t n, int64_t k, int64_t* kept,
                           float* margin, uint32_t* keys, cudaStream_t st) {
     select_kernel<<<1, kSelThreads, 0, st>>>(scores, B, n, k, kept, margin, keys);
+    return counted(cudaGetLastError(), 1);
+}
+
+cudaError_t launch_select_compact(const float* scores, int64_t B, int64_t num_pages, int64_t k,
+                                  int64_t* kept, float* margin, uint32_t* keys, int64_t* pt,
+                                  int64_t sink_pages, int64_t tail_first, int64_t n_total,
+                                  int64_t* free_stack, int64_t free_top, cudaStream_t st) {
+    select_compact_kernel<<<1, kSelThreads, 0, st>>>(scores, B, num_pages, k, kept, margin, keys,
+                                                       pt, sink_pages, tail_first, n_total,
+                                                       free_stack, free_top);
     return counted(cudaGetLastError(), 1);
 }
 

@@ -119,6 +119,9 @@ struct FusedParams {
     // head-sharded (partial) scoring: instead of updating the salience, write the signed
     // resonance keys of the local heads and the appended token's kv-head norms here
     Exchange xc;
+    // score-only pass of a compacting step: page scores [B][pool_num] (row stride pool_num)
+    // of logical pages pool_first .. pool_first + pool_num - 1 (pool == nullptr: none)
+    float* pool; int64_t pool_first, pool_num;
 };
 
 cudaError_t launch_score(const ScoreParams& p, cudaStream_t st);
@@ -130,6 +133,10 @@ cudaError_t launch_pool(const float* sal, int64_t B, int64_t S, int64_t stride_b
 cudaError_t launch_page_scores(const PageScoreParams& p, cudaStream_t st);
 cudaError_t launch_select(const float* scores, int64_t B, int64_t n, int64_t k, int64_t* kept,
                           float* margin, uint32_t* keys, cudaStream_t st);
+cudaError_t launch_select_compact(const float* scores, int64_t B, int64_t num_pages, int64_t k,
+                                  int64_t* kept, float* margin, uint32_t* keys, int64_t* pt,
+                                  int64_t sink_pages, int64_t tail_first, int64_t n_total,
+                                  int64_t* free_stack, int64_t free_top, cudaStream_t st);
 cudaError_t launch_compact_pages(int64_t* pt, int64_t sink_pages, int64_t num_pages,
                                  const int64_t* kept, int64_t k, int64_t tail_first,
                                  int64_t n_total, int64_t* free_stack, int64_t free_top,

@@ -5,9 +5,8 @@ of the Qwen-7B-shaped workload at batch 1 and 128k context) is drawn on the CPU 
 copied to the GPU and driven through ``PagedRazorKVCache`` with the decode-step protocol the
 benchmark uses (prefill with ``update``, then ``decode_step`` per layer and step).  Every
 compaction decision is recorded and compared with the reference's (fixture): same layer,
-cached length, budget, page count and k, and the same kept pages.  A different kept set is
-accepted only at a provable near-tie (the gap at the cut within 4e-6 of the largest salience),
-in which case the cache follows the reference's set; the count is reported.
+cached length, budget, page count and k, and the same kept pages (a mismatch is reported with
+whether it was a provable near-tie, the gap at the cut within 4e-6 of the largest salience).
 
 The oracle runs beside the GPU on the layers it can afford here (both Qwen-shaped layers,
 Llama-shaped layer 0): salience and retained K must equal it bit for bit after the last
@@ -45,23 +44,9 @@ def test_cuda_keeps_the_reference_pages_at_scale(name):
                       pyramid_mode=w.pyramid_mode, pyramid_min_ratio=w.pyramid_min_ratio,
                       pyramid_max_ratio=w.pyramid_max_ratio)
     cache = PagedRazorKVCache(cfg, w.num_layers)
+    # the production path (fused score + pool pass, fused select + compact); decisions are
+    # recorded and compared after the run
     cache.record_decisions = True
-    excused = []
-
-    def follow(layer, i, kept, margin):
-        d = ref[i]
-        assert d["layer"] == layer, f"decision {i}: layer {layer}, reference {d['layer']}"
-        got = kept.cpu().numpy()
-        if np.array_equal(got, d["kept"]):
-            return None
-        scale = float(cache.salience_scores[layer].abs().max())
-        assert near_tie(d["margin"], scale) or near_tie(float(margin.item()), scale), (
-            f"decision {i} (layer {layer}): kept pages differ at margin {float(margin.item()):.3e}"
-            f" (reference {d['margin']:.3e})")
-        excused.append(i)
-        return torch.from_numpy(d["kept"])
-
-    cache.kept_override = follow
 
     olayers = ORACLE_LAYERS[name]
     ocache = O.OracleCache(oracle_config(w), w.num_layers, elt_size(w.dtype))
@@ -98,7 +83,12 @@ def test_cuda_keeps_the_reference_pages_at_scale(name):
     for i, (d, r) in enumerate(zip(cache.decisions, ref)):
         assert (d.layer, d.seq_len, d.budget, d.num_pages, d.k) == (
             r["layer"], r["seq_len"], r["budget"], r["num_pages"], r["k"]), f"decision {i}"
-        assert np.array_equal(d.kept.cpu().numpy(), r["kept"]), f"decision {i}"
+        if not np.array_equal(d.kept.cpu().numpy(), r["kept"]):
+            scale = float(cache.salience_scores[d.layer].abs().max())
+            tie = near_tie(r["margin"], scale) or near_tie(float(d.margin.item()), scale)
+            raise AssertionError(f"decision {i} (layer {d.layer}): kept pages differ from the "
+                                 f"reference at margin {float(d.margin.item()):.3e} (reference "
+                                 f"{r['margin']:.3e}; {'a' if tie else 'not a'} provable near-tie)")
     for layer in case["layers"]:
         assert cache.get_cached_seq_length(layer) == g["len"][layer]
         S = cache.salience_scores[layer].cpu().numpy()
@@ -107,6 +97,4 @@ def test_cuda_keeps_the_reference_pages_at_scale(name):
             assert np.array_equal(S.view(np.uint32), ocache.S[layer].view(np.uint32)), layer
             Kg = cache.key_cache[layer].float().cpu().numpy()
             assert np.array_equal(Kg, ocache.K[layer]), layer
-    print(f"{name}: {len(ref)} decisions equal to the reference, {len(excused)} near-tie "
-          f"decisions followed")
-    assert len(excused) <= 1
+    print(f"{name}: {len(ref)} decisions equal to the reference")
