@@ -61,10 +61,12 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=0,
                     help="time K evenly spaced layers of the model only (for caches larger "
                          "than one GPU's memory); the JSON config records the subset")
-    ap.add_argument("--shard", default="auto", choices=["auto", "batch", "heads"],
-                    help="multi-GPU split: by sequence (weak scaling, batch per GPU fixed) or by "
-                         "kv head (strong scaling, one batch split over the GPUs' heads); auto "
-                         "splits heads when the batch is smaller than the GPU count")
+    ap.add_argument("--shard", default="auto", choices=["auto", "batch", "split", "heads"],
+                    help="multi-GPU split: 'batch' gives every GPU the workload's batch of its "
+                         "own sequences (weak scaling); 'split' divides the workload's batch "
+                         "over the GPUs (strong scaling); 'heads' gives every GPU some kv heads "
+                         "of the same sequences (strong scaling); auto splits heads when the "
+                         "batch is smaller than the GPU count, else 'batch'")
     ap.add_argument("--event-every", type=int, default=8,
                     help="record per-launch CUDA events on every k-th timed step")
     return ap.parse_args()
@@ -383,10 +385,12 @@ def workload_config(w, n, shard="batch"):
         "kv_heads": w.num_kv_heads, "head_dim": w.head_dim,
         "batch_per_gpu": w.batch, "global_batch": w.batch if heads else w.batch * n,
         "kv_heads_per_gpu": w.num_kv_heads // n if heads else w.num_kv_heads,
+        "shard": shard,
         "context": w.context, "page_size": w.page_size,
         "sink": w.sink_tokens, "window": w.local_window,
         "pyramid": f"{w.pyramid_mode} {w.pyramid_min_ratio}->{w.pyramid_max_ratio}",
-        "parallelism": (f"kv-head-sharded x{n}" if heads else f"batch-sharded x{n}")
+        "parallelism": (f"kv-head-sharded x{n}" if heads else
+                        f"batch-split x{n}" if shard == "split" else f"batch-sharded x{n}")
                        if n > 1 else "single GPU",
         "l2": "inputs larger than L2 (retained KV per step >> 126 MB)",
     }
@@ -511,6 +515,14 @@ def main():
         wr = w
         h0 = rank * (w.num_kv_heads // world)
         hkv = w.num_kv_heads // world
+    elif shard == "split":
+        # the workload's batch divided over the ranks (strong scaling); each rank draws its own
+        # sequences, and selection still averages over the whole batch (all-gather)
+        if w.batch % world:
+            raise SystemExit(f"--shard split: batch {w.batch} does not divide over {world} GPUs")
+        w = w.scaled(batch=w.batch // world)
+        wr = w.scaled(seed=w.seed + 1000 * rank)
+        h0, hkv = 0, w.num_kv_heads
     else:
         # each rank holds its own sequences (weak scaling): a distinct seed per rank
         wr = w.scaled(seed=w.seed + 1000 * rank)
@@ -529,7 +541,7 @@ def main():
     total_steps = args.warmup + args.steps + args.e2e_steps
     cache = PagedRazorKVCache(cfg, L, max_slots=pool_slots(w, cfg, total_steps, layers))
 
-    if shard == "batch":
+    if shard in ("batch", "split"):
         from razorkv_b200.distributed import batch_sharded_score_reducer
         cache.score_reducer = batch_sharded_score_reducer()
     elif shard == "heads":
@@ -721,7 +733,7 @@ def main():
         "warmup": args.warmup,
         "ms_per_step": ms / args.steps,
         "higher_is_better": True,
-        "scaling": "strong" if shard == "heads" else "weak",
+        "scaling": "strong" if shard in ("heads", "split") else "weak",
         "vs_baseline": None,
         "dtype": "bf16" if w.dtype == torch.bfloat16 else "fp32",
         "data": "synthetic: seeded N(0,1) K/V/q, 1% planted query-aligned pages per head",

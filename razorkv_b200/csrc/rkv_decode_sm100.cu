@@ -785,15 +785,12 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                         for (int r = 0; r < 4; ++r) {
                             tr[r] = 4 * r + g;
                             rem[r] = __shfl_sync(0xffffffffu, r < 2 ? mA : mB, (tr[r] & 7) * 4);
-                            hr[r] = rem[r] ? __ffs(rem[r]) - 1 : 0;
+                            keyr[r] = 0u;
                         }
-                        canon_dots4<T, D>(kb, a.half_bytes, tr, qb, hr, j, a.scale_r, vr);
-#pragma unroll
-                        for (int r = 0; r < 4; ++r) {
-                            keyr[r] = rem[r] ? ordered_key(vr[r]) : 0u;
-                            rem[r] &= rem[r] - 1u;
-                        }
-                        while (__any_sync(0xffffffffu, (rem[0] | rem[1] | rem[2] | rem[3]) != 0u)) {
+                        // one copy of the round body (instruction fetch is a limiter here):
+                        // the first pass takes every token's lowest candidate, later passes the
+                        // rest (rare)
+                        do {
 #pragma unroll
                             for (int r = 0; r < 4; ++r) hr[r] = rem[r] ? __ffs(rem[r]) - 1 : 0;
                             canon_dots4<T, D>(kb, a.half_bytes, tr, qb, hr, j, a.scale_r, vr);
@@ -802,7 +799,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                                 if (rem[r]) keyr[r] = max(keyr[r], ordered_key(vr[r]));
                                 rem[r] &= rem[r] - 1u;
                             }
-                        }
+                        } while (__any_sync(0xffffffffu, (rem[0] | rem[1] | rem[2] | rem[3]) != 0u));
                         if (j == 0) {
 #pragma unroll
                             for (int r = 0; r < 4; ++r) sm.red[slot][warp][4 * r + g] = keyr[r];
