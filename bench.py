@@ -67,6 +67,9 @@ def parse_args():
                          "over the GPUs (strong scaling); 'heads' gives every GPU some kv heads "
                          "of the same sequences (strong scaling); auto splits heads when the "
                          "batch is smaller than the GPU count, else 'batch'")
+    ap.add_argument("--no-peer-exchange", action="store_true",
+                    help="with --shard heads, exchange salience shares by NCCL all-reduce "
+                         "instead of peer stores over NVLink")
     ap.add_argument("--event-every", type=int, default=8,
                     help="record per-launch CUDA events on every k-th timed step")
     return ap.parse_args()
@@ -547,6 +550,10 @@ def main():
     elif shard == "heads":
         from razorkv_b200.distributed import kv_head_shard
         cache.head_group = kv_head_shard(w.num_kv_heads)
+        if not args.no_peer_exchange:
+            # decode steps exchange by peer stores over NVLink (no collective); the bound
+            # covers every layer's retained tokens over the run
+            cache.head_group.enable_peer_exchange(dev, B, w.context + total_steps + 64)
 
     def local(q, k, v):
         """This rank's heads of one step's (or the prefill's) tensors."""

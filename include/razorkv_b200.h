@@ -34,6 +34,8 @@
  *                             max-pool of a compacting decode step, one pass over K)
  *   rkv_select_compact_pages  razorkv/cache.py:333-359 (selection and pointer-only
  *                             compaction in one launch)
+ *   rkv_append_decode_peer,   the head-sharded step with the exchange by peer stores over
+ *   rkv_salience_apply_peer   NVLink instead of a collective (same reference lines)
  *   rkv_append_partial,       the same steps (razorkv/cache.py:239-287, 361-393) for a rank
  *   rkv_score_partial,        that holds only some kv heads of a layer: each writes its share
  *   rkv_append_decode_partial of the salience update to an exchange block, and
@@ -341,6 +343,47 @@ int rkv_append_decode_partial(const rkv_kv_layout* kv,
 int rkv_salience_apply(const rkv_kv_layout* kv, const rkv_salience* sal, const rkv_exchange* xc,
                        int64_t score_tokens, int64_t new_first, int64_t n_new,
                        int salience_init, float decay, float one_minus_decay, void* stream);
+
+/* The exchange without a collective (no reference counterpart; ranks on one node with peer
+ * access over NVLink).  Every rank owns a region of two buffers x nranks sub-blocks of `sub`
+ * int32 (a sub-block laid out as the rkv_exchange block: rows of stride_b per sequence) and
+ * nranks uint32 flags, and every rank can address every other rank's region and flags
+ * (CUDA IPC).  rkv_append_decode_peer stores this rank's share into sub-block `rank` of
+ * buffer buf_off of every rank's region -- plain stores into peer memory, no multicast --
+ * and its last CTA then releases flags[r][rank] = epoch on every rank r.
+ * rkv_salience_apply_peer waits (bounded, about a second; on timeout it sets the workspace
+ * error flag to 1 and leaves the salience alone) until every flag of this rank has reached
+ * the epoch and applies the update from the MAX over the sub-blocks.  The caller advances the
+ * epoch by one per exchange and alternates the two buffers (buf_off = (epoch & 1) * nranks *
+ * sub), so a rank never overwrites a sub-block a peer may still be reading. */
+typedef struct rkv_peer_exchange {
+    int32_t* const* regions;     /* device array [nranks]: each rank's region, as seen here */
+    uint32_t* const* flags;      /* device array [nranks]: each rank's flags, as seen here */
+    const int32_t* my_region;    /* this rank's region */
+    const uint32_t* my_flags;    /* this rank's flags */
+    int32_t rank, nranks;
+    int64_t sub;                 /* int32 elements per sub-block */
+    int64_t buf_off;             /* int32 elements to the buffer of this exchange */
+    uint32_t epoch;              /* 1, 2, 3, ... */
+    uint32_t reserved;
+} rkv_peer_exchange;
+
+/* rkv_append_decode_partial with the share stored to every rank (xc gives the block layout:
+ * stride_b, norm_off, head0, num_kv_heads_total; xc->x is not used).  Fused decode shapes
+ * only (RKV_ERR_UNSUPPORTED otherwise; use the collective path then). */
+int rkv_append_decode_peer(const rkv_kv_layout* kv, const void* k_new, const void* v_new,
+                           int64_t new_stride_b, int64_t new_stride_h, int64_t* page_table,
+                           const int64_t* free_stack, int64_t free_top, int salience_init,
+                           const rkv_query* q, float scale, const rkv_output* out,
+                           const rkv_exchange* xc, const rkv_peer_exchange* px, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+/* rkv_salience_apply on the MAX over the sub-blocks of this rank's region, after the wait. */
+int rkv_salience_apply_peer(const rkv_kv_layout* kv, const rkv_salience* sal,
+                            const rkv_exchange* xc, const rkv_peer_exchange* px,
+                            int64_t score_tokens, int64_t new_first, int64_t n_new,
+                            int salience_init, float decay, float one_minus_decay,
+                            void* workspace, size_t workspace_bytes, void* stream);
 
 /* dst[b, h, t, :] = row (b, h, t) of kv (K when which == 0, V when 1), t < num_tokens;
  * dst is contiguous [B, Hkv, num_tokens, D] of kv->dtype.  sal_dst (optional, [B, num_tokens])

@@ -58,6 +58,12 @@ class Exchange(ctypes.Structure):
                 ("num_kv_heads_total", c_i32)]
 
 
+class PeerExchange(ctypes.Structure):
+    _fields_ = [("regions", c_vp), ("flags", c_vp), ("my_region", c_vp), ("my_flags", c_vp),
+                ("rank", c_i32), ("nranks", c_i32), ("sub", c_i64), ("buf_off", c_i64),
+                ("epoch", ctypes.c_uint32), ("reserved", ctypes.c_uint32)]
+
+
 P = ctypes.POINTER
 
 # name -> (restype, argtypes); mirrors include/razorkv_b200.h
@@ -108,6 +114,12 @@ _SIGNATURES = {
                                                  P(Output), P(Exchange), c_vp, c_sz, c_vp]),
     "rkv_salience_apply": (ctypes.c_int, [P(KVLayout), P(Salience), P(Exchange), c_i64, c_i64,
                                           c_i64, ctypes.c_int, c_f32, c_f32, c_vp]),
+    "rkv_append_decode_peer": (ctypes.c_int, [P(KVLayout), c_vp, c_vp, c_i64, c_i64, c_vp, c_vp,
+                                              c_i64, ctypes.c_int, P(Query), c_f32, P(Output),
+                                              P(Exchange), P(PeerExchange), c_vp, c_sz, c_vp]),
+    "rkv_salience_apply_peer": (ctypes.c_int, [P(KVLayout), P(Salience), P(Exchange),
+                                               P(PeerExchange), c_i64, c_i64, c_i64, ctypes.c_int,
+                                               c_f32, c_f32, c_vp, c_sz, c_vp]),
     "rkv_append_score_pool": (ctypes.c_int, [P(KVLayout), P(Salience), c_vp, c_vp, c_i64, c_i64,
                                              c_vp, c_vp, c_i64, ctypes.c_int, P(Query), c_f32,
                                              c_f32, c_i64, c_i64, c_vp, c_vp]),

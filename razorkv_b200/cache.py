@@ -862,16 +862,32 @@ class PagedRazorKVCache(BaseCacheClass):
         obs = self.launch_observer
         if obs is not None:
             obs.before(layer_idx, 2 * B * self._Hkv * cur * D * self._elt)
+        peer = None
         if self.head_group is not None:
-            # head-sharded: keys and norms to the exchange block, then the MAX over the group
-            # and the salience update (below, once the token count is advanced)
-            self._xbegin(layer_idx, score_tokens=cur, new_first=n0, n_new=1)
-            st = self._lib.rkv_append_decode_partial(
-                lay, k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1), pt.data_ptr(),
-                self._free.data_ptr(), self._free_top, self._sal_init, qs,
-                float(scaling) if scaling else 0.0, os_, self._xpend[2], ws.data_ptr(),
-                ws.numel(), stream)
-            what = "rkv_append_decode_partial"
+            hg = self.head_group
+            if hg.peer is not None and cur + hg.num_kv_heads_total <= hg.peer.stride:
+                # head-sharded over NVLink: the kernel stores its share into every rank's
+                # region; the update below waits on the ranks' flags (no collective)
+                peer = hg.peer.next()
+                xc = Exchange(0, hg.peer.stride, cur, hg.head0, hg.num_kv_heads_total)
+                st = self._lib.rkv_append_decode_peer(
+                    lay, k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1), pt.data_ptr(),
+                    self._free.data_ptr(), self._free_top, self._sal_init, qs,
+                    float(scaling) if scaling else 0.0, os_, xc, peer, ws.data_ptr(),
+                    ws.numel(), stream)
+                what = "rkv_append_decode_peer"
+                if st == 2:   # not a fused-kernel shape: every rank takes the collective path
+                    peer = None
+            if peer is None:
+                # head-sharded: keys and norms to the exchange block, then the MAX over the
+                # group and the salience update (below, once the token count is advanced)
+                self._xbegin(layer_idx, score_tokens=cur, new_first=n0, n_new=1)
+                st = self._lib.rkv_append_decode_partial(
+                    lay, k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1), pt.data_ptr(),
+                    self._free.data_ptr(), self._free_top, self._sal_init, qs,
+                    float(scaling) if scaling else 0.0, os_, self._xpend[2], ws.data_ptr(),
+                    ws.numel(), stream)
+                what = "rkv_append_decode_partial"
         else:
             st = self._lib.rkv_append_decode(
                 lay, self._sal_struct, k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1),
@@ -887,7 +903,12 @@ class PagedRazorKVCache(BaseCacheClass):
         self._n[layer_idx] = cur
         self._seen_tokens = seen
         self._layers[layer_idx].cumulative_length = seen
-        if self.head_group is not None:
+        if peer is not None:
+            st = self._lib.rkv_salience_apply_peer(
+                self._layout(layer_idx), self._sal_struct, xc, peer, cur, n0, 1, self._sal_init,
+                decay, 1.0 - decay, ws.data_ptr(), ws.numel(), stream)
+            check(st, "rkv_salience_apply_peer")
+        elif self.head_group is not None:
             self._settle()
         return out
 

@@ -458,6 +458,84 @@ int rkv_append_decode_partial(const rkv_kv_layout* kv,
     return rkv_decode_attention(q, &grown, scale, 0, out, workspace, workspace_bytes, stream);
 }
 
+static int peer_status(const rkv_peer_exchange* px) {
+    if (!px || !px->regions || !px->flags || !px->my_region || !px->my_flags) return RKV_ERR_INVALID_ARGUMENT;
+    if (px->nranks < 1 || px->rank < 0 || px->rank >= px->nranks || px->sub < 1 || px->buf_off < 0)
+        return RKV_ERR_INVALID_ARGUMENT;
+    return RKV_OK;
+}
+
+int rkv_append_decode_peer(const rkv_kv_layout* kv, const void* k_new, const void* v_new,
+                           int64_t new_stride_b, int64_t new_stride_h, int64_t* page_table,
+                           const int64_t* free_stack, int64_t free_top, int salience_init,
+                           const rkv_query* q, float scale, const rkv_output* out,
+                           const rkv_exchange* xc, const rkv_peer_exchange* px, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+    if (!kv || !xc) return RKV_ERR_INVALID_ARGUMENT;
+    rkv_kv_layout grown = *kv;
+    grown.num_tokens = kv->num_tokens + 1;
+    int st = check_kv(&grown, true);
+    if (st) return st;
+    if ((st = check_q(q, &grown))) return st;
+    if ((st = peer_status(px))) return st;
+    if (xc->stride_b < grown.num_tokens || xc->norm_off < grown.num_tokens ||
+        xc->norm_off + xc->num_kv_heads_total > xc->stride_b || xc->head0 < 0 ||
+        xc->head0 + kv->num_kv_heads > xc->num_kv_heads_total ||
+        px->sub < grown.batch * xc->stride_b)
+        return RKV_ERR_INVALID_ARGUMENT;
+    if (!out || !out->out) return RKV_ERR_INVALID_ARGUMENT;
+    const bool rows_aligned = k_new && v_new && !(reinterpret_cast<uintptr_t>(k_new) & 15) &&
+                              !(reinterpret_cast<uintptr_t>(v_new) & 15) &&
+                              !((new_stride_b * 2) & 15) && !((new_stride_h * 2) & 15);
+    if (!(page_table && free_stack && grown.batch > 0 && grown.page_table == page_table &&
+          grown.pt_stride_b == 0 && rows_aligned && fast_ok(q, &grown, true) &&
+          (kv->num_tokens % kv->page_size != 0 || free_top >= 1)))
+        return RKV_ERR_UNSUPPORTED;
+    if (workspace_bytes < rkv_decode_fused_workspace_size(q, &grown) || !workspace)
+        return RKV_ERR_WORKSPACE_TOO_SMALL;
+    FusedParams p = fused_params(q, &grown, nullptr, 0.f, 0.f, scale, out);
+    p.partials = ws_body(workspace); p.counters = ws_counters(workspace); p.err = ws_err(workspace);
+    p.k_new = k_new; p.v_new = v_new; p.new_stride_b = new_stride_b;
+    p.new_stride_h = new_stride_h; p.pt_w = page_table; p.free_stack = free_stack;
+    p.free_top = free_top; p.sal_init_norm = salience_init == RKV_SAL_NORM;
+    p.xc = exchange_of(xc);
+    p.xc.x = const_cast<int32_t*>(px->my_region);   // marks the partial mode
+    p.xc.regions = px->regions; p.xc.flags = px->flags;
+    p.xc.rank = px->rank; p.xc.nranks = px->nranks; p.xc.sub = px->sub;
+    p.xc.buf_off = px->buf_off; p.xc.epoch = px->epoch;
+    return status_of(launch_fused(p, S(stream)));
+}
+
+int rkv_salience_apply_peer(const rkv_kv_layout* kv, const rkv_salience* sal,
+                            const rkv_exchange* xc, const rkv_peer_exchange* px,
+                            int64_t score_tokens, int64_t new_first, int64_t n_new,
+                            int salience_init, float decay, float one_minus_decay,
+                            void* workspace, size_t workspace_bytes, void* stream) {
+    if (!kv || !sal || !sal->s || !xc) return RKV_ERR_INVALID_ARGUMENT;
+    int st = peer_status(px);
+    if (st) return st;
+    if (kv->batch < 0 || (kv->page_table && kv->page_size < 1)) return RKV_ERR_INVALID_ARGUMENT;
+    if (score_tokens < 0 || new_first < 0 || n_new < 0) return RKV_ERR_INVALID_ARGUMENT;
+    const int64_t end = score_tokens > new_first + n_new ? score_tokens : new_first + n_new;
+    if (end > kv->num_tokens || xc->stride_b < score_tokens || xc->num_kv_heads_total < 1 ||
+        px->sub < kv->batch * xc->stride_b ||
+        (salience_init == RKV_SAL_NORM && n_new > 0 &&
+         xc->stride_b < xc->norm_off + n_new * xc->num_kv_heads_total))
+        return RKV_ERR_INVALID_ARGUMENT;
+    if (!workspace || workspace_bytes < RKV_WORKSPACE_HEADER_BYTES) return RKV_ERR_WORKSPACE_TOO_SMALL;
+    PeerApplyParams p{};
+    p.sal = sal->s; p.sal_stride_b = sal->stride_b; p.sal_stride_p = sal->stride_p;
+    p.page_table = kv->page_table; p.page_size = kv->page_size; p.B = kv->batch;
+    p.region = px->my_region; p.flags = px->my_flags; p.nranks = px->nranks; p.sub = px->sub;
+    p.buf_off = px->buf_off; p.epoch = px->epoch; p.stride_b = xc->stride_b;
+    p.norm_off = xc->norm_off; p.htot = xc->num_kv_heads_total;
+    p.score_tokens = score_tokens; p.new_first = new_first; p.n_new = n_new;
+    p.norm_init = salience_init == RKV_SAL_NORM; p.decay = decay; p.one_minus_decay = one_minus_decay;
+    p.err = ws_err(workspace);
+    p.wait_limit = 2000000000LL;   // ~1 s at B200 clocks
+    return status_of(launch_apply_peer(p, S(stream)));
+}
+
 int rkv_salience_apply(const rkv_kv_layout* kv, const rkv_salience* sal, const rkv_exchange* xc,
                        int64_t score_tokens, int64_t new_first, int64_t n_new,
                        int salience_init, float decay, float one_minus_decay, void* stream) {

@@ -447,18 +447,29 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                                 // appended token's kv-head norms go to the exchange block; the
                                 // salience is updated after the MAX over the ranks
                                 const int64_t tt = tile * kTileTokens + t;
-                                int32_t* xr = a.xc.x + b * a.xc.stride_b;
+                                // the local block, or this rank's sub-block of every rank's
+                                // region (peer stores over NVLink)
+                                const int nr = a.xc.regions ? a.xc.nranks : 1;
+                                const int64_t off = a.xc.buf_off + (int64_t)a.xc.rank * a.xc.sub +
+                                                    b * a.xc.stride_b;
                                 if (tt < a.score_n) {
                                     uint32_t key = 0u;
                                     for (int hh = 0; hh < Hkv; ++hh) key = max(key, sm.red[slot][s * Hkv + hh][t]);
-                                    xr[tt] = signed_key_of(key);
+                                    const int32_t sk = signed_key_of(key);
+                                    for (int r = 0; r < nr; ++r) {
+                                        int32_t* xr = a.xc.regions ? a.xc.regions[r] + off : a.xc.x + b * a.xc.stride_b;
+                                        xr[tt] = sk;
+                                    }
                                 }
                                 if (append && tile == new_tile && t == new_row) {
-                                    for (int hh = 0; hh < a.xc.htot; ++hh) {
-                                        const int lh = hh - a.xc.h0;
-                                        xr[a.xc.norm_off + hh] =
-                                            (lh >= 0 && lh < Hkv) ? signed_key_of(ordered_key(sm.new_norm[slot][s][lh]))
-                                                                  : INT32_MIN;
+                                    for (int r = 0; r < nr; ++r) {
+                                        int32_t* xr = a.xc.regions ? a.xc.regions[r] + off : a.xc.x + b * a.xc.stride_b;
+                                        for (int hh = 0; hh < a.xc.htot; ++hh) {
+                                            const int lh = hh - a.xc.h0;
+                                            xr[a.xc.norm_off + hh] =
+                                                (lh >= 0 && lh < Hkv) ? signed_key_of(ordered_key(sm.new_norm[slot][s][lh]))
+                                                                      : INT32_MIN;
+                                        }
                                     }
                                 }
                                 continue;
@@ -504,6 +515,23 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                     if (++slot == NS) { slot = 0; par ^= 1u; }
                 }
                 pos = seg_end;
+            }
+            if constexpr (XCH) {
+                if (a.xc.regions) {
+                    // peer exchange: once every CTA's stores are out, the last CTA releases
+                    // this rank's flag on every rank (the ticket returns to zero)
+                    __syncwarp();
+                    if (lane == 0) {
+                        __threadfence_system();
+                        const int ticket = atomicAdd(a.counters, 1);
+                        if (ticket == (int)gridDim.x - 1) {
+                            __threadfence_system();
+                            for (int r = 0; r < a.xc.nranks; ++r)
+                                st_release_sys(a.xc.flags[r] + a.xc.rank, a.xc.epoch);
+                            atomicExch(a.counters, 0);
+                        }
+                    }
+                }
             }
             return;
         }

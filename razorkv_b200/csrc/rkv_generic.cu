@@ -663,8 +663,79 @@ __global__ void apply_kernel(ApplyParams p) {
 }
 
 // ------------------------------------------------------------------------------------------
+// The same update when the ranks' shares arrived by peer stores (KV-head sharding over
+// NVLink): this rank's region holds one sub-block per rank, and every rank's decode kernel
+// releases its flag here once its stores are out.  Thread 0 of each CTA waits (bounded) for
+// every flag to reach the epoch; then every thread acquires the flags itself and reads the
+// MAX over the sub-blocks.  On timeout the CTA records error 1 and leaves the salience alone.
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__global__ void apply_peer_kernel(PeerApplyParams p) {
+    __shared__ int s_ok;
+    if (threadIdx.x == 0) {
+        bool ok = true;
+        const long long t0 = clock64();
+        for (int r = 0; r < p.nranks && ok; ++r) {
+            while ((int32_t)(ld_acquire_sys_u32(p.flags + r) - p.epoch) < 0) {
+                if (clock64() - t0 > p.wait_limit) { ok = false; break; }
+            }
+        }
+        if (!ok && p.err) atomicExch(p.err, 1);
+        s_ok = ok ? 1 : 0;
+    }
+    __syncthreads();
+    if (!s_ok) return;
+    for (int r = 0; r < p.nranks; ++r) (void)ld_acquire_sys_u32(p.flags + r);
+    const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int64_t b = blockIdx.y;
+    const int64_t end = max(p.score_tokens, p.new_first + p.n_new);
+    if (t >= end) return;
+    const int32_t* base = p.region + p.buf_off + b * p.stride_b;
+    float* sp = p.sal + (p.page_table ? p.page_table[t / p.page_size] * p.sal_stride_p +
+                                            b * p.sal_stride_b + t % p.page_size
+                                      : b * p.sal_stride_b + t);
+    const bool is_new = t >= p.new_first && t < p.new_first + p.n_new;
+    float old;
+    if (is_new) {
+        old = 1.0f;
+        if (p.norm_init) {
+            const int64_t nb = p.norm_off + (t - p.new_first) * p.htot;
+            float acc = 0.0f;
+            for (int h = 0; h < p.htot; ++h) {
+                int32_t k = INT32_MIN;
+                for (int r = 0; r < p.nranks; ++r) k = max(k, base[r * p.sub + nb + h]);
+                acc = __fadd_rn(acc, key_to_float(ordered_of(k)));
+            }
+            old = __fdiv_rn(acc, (float)p.htot);
+        }
+    } else {
+        old = *sp;
+    }
+    if (t < p.score_tokens) {
+        int32_t k = INT32_MIN;
+        for (int r = 0; r < p.nranks; ++r) k = max(k, base[r * p.sub + t]);
+        *sp = __fadd_rn(__fmul_rn(p.decay, old), __fmul_rn(p.one_minus_decay, key_to_float(ordered_of(k))));
+    } else if (is_new) {
+        *sp = old;
+    }
+}
+
+// ------------------------------------------------------------------------------------------
 // launchers
 // ------------------------------------------------------------------------------------------
+cudaError_t launch_apply_peer(const PeerApplyParams& p, cudaStream_t st) {
+    const int64_t end = p.score_tokens > p.new_first + p.n_new ? p.score_tokens : p.new_first + p.n_new;
+    if (end <= 0 || p.B <= 0) return cudaSuccess;
+    dim3 grid((unsigned)((end + 255) / 256), (unsigned)p.B);
+    apply_peer_kernel<<<grid, 256, 0, st>>>(p);
+    return counted(cudaGetLastError(), 1);
+}
+
 cudaError_t launch_apply(const ApplyParams& p, cudaStream_t st) {
     const int64_t end = p.score_tokens > p.new_first + p.n_new ? p.score_tokens : p.new_first + p.n_new;
     if (end <= 0 || p.B <= 0) return cudaSuccess;

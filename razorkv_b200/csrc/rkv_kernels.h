@@ -19,6 +19,23 @@ inline cudaError_t counted(cudaError_t e, int n) {
 // kv-head norms of the i-th appended token.  x == nullptr: the salience is updated in place.
 struct Exchange {
     int32_t* x; int64_t stride_b, norm_off; int h0, htot;
+    // peer exchange (regions != nullptr): instead of x, write into region r + buf_off +
+    // rank * sub of every rank r (peer memory over NVLink; r == rank is local), then the last
+    // CTA releases flags[r][rank] = epoch on every rank
+    int32_t* const* regions; uint32_t* const* flags;
+    int rank, nranks; int64_t sub, buf_off; uint32_t epoch;
+};
+
+// rkv_salience_apply_peer: as ApplyParams, the exchange block being the max over the nranks
+// sub-blocks of this rank's region once every rank's flag has reached the epoch.
+struct PeerApplyParams {
+    float* sal; int64_t sal_stride_b, sal_stride_p;
+    const int64_t* page_table; int64_t page_size; int64_t B;
+    const int32_t* region; const uint32_t* flags; int nranks; int64_t sub, buf_off;
+    uint32_t epoch; int64_t stride_b, norm_off; int htot;
+    int64_t score_tokens, new_first, n_new;
+    int norm_init; float decay, one_minus_decay;
+    int* err; long long wait_limit;
 };
 
 // Signed key of an fp32 value: the order-preserving uint32 key with its top bit flipped, so
@@ -147,6 +164,7 @@ cudaError_t launch_release(const int64_t* pages, int64_t n, int64_t* free_stack,
                            cudaStream_t st);
 cudaError_t launch_gather(const GatherParams& p, cudaStream_t st);
 cudaError_t launch_apply(const ApplyParams& p, cudaStream_t st);
+cudaError_t launch_apply_peer(const PeerApplyParams& p, cudaStream_t st);
 
 // fast path: returns cudaErrorNotSupported when the shape is outside its coverage
 bool fused_supported(int dtype, int D, int Hkv, int Hq, int64_t page_size, int64_t stride_t,

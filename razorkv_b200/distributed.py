@@ -59,10 +59,66 @@ class HeadGroup:
         self.num_kv_heads_local = num_kv_heads_local
         self.num_kv_heads_total = num_kv_heads_total
         self.group = group
+        self.peer = None   # PeerExchange once enable_peer_exchange has run
 
     def reduce(self, x: torch.Tensor) -> None:
         """Element-wise MAX of the int32 exchange block over the ranks of the group, in place."""
         dist.all_reduce(x, op=dist.ReduceOp.MAX, group=self.group)
+
+    def enable_peer_exchange(self, device, batch: int, max_tokens: int) -> "PeerExchange":
+        """Set up the exchange without a collective for decode steps of up to max_tokens
+        tokens per layer (a collective call: every rank of the group calls it).  Each rank
+        allocates a region of two buffers x world sub-blocks of batch x (max_tokens + kv heads)
+        int32 plus world flags, and maps every other rank's region into this process through
+        CUDA IPC; the decode kernel then stores its share straight into every rank's region
+        over NVLink and the salience update waits on the flags instead of an all-reduce.
+        Steps longer than max_tokens fall back to ``reduce``."""
+        self.peer = PeerExchange(self, torch.device(device), batch, max_tokens)
+        return self.peer
+
+
+class PeerExchange:
+    """The ranks' exchange regions mapped into this process (see HeadGroup)."""
+
+    def __init__(self, hg: HeadGroup, device: torch.device, batch: int, max_tokens: int):
+        from torch.multiprocessing.reductions import reduce_tensor
+
+        from ._lib import PeerExchange as PX
+
+        world = dist.get_world_size(hg.group)
+        rank = dist.get_rank(hg.group)
+        self.world, self.rank = world, rank
+        self.stride = max_tokens + hg.num_kv_heads_total
+        self.sub = batch * self.stride
+        n_data = 2 * world * self.sub
+        self.flag_off = (n_data + 63) // 64 * 64          # int32 elements
+        self.region = torch.zeros(self.flag_off + 64 * ((world + 63) // 64), dtype=torch.int32,
+                                  device=device)
+        torch.cuda.synchronize(device)
+        rebuild, args = reduce_tensor(self.region)
+        handles = [None] * world
+        dist.all_gather_object(handles, args, group=hg.group)
+        # keep every mapped peer region alive as long as this object
+        self.mapped = [self.region if r == rank else rebuild(*handles[r]) for r in range(world)]
+        base = [t.data_ptr() for t in self.mapped]
+        self.regions = torch.tensor(base, dtype=torch.int64, device=device)
+        self.flags = torch.tensor([b + 4 * self.flag_off for b in base], dtype=torch.int64,
+                                  device=device)
+        self.epoch = 0
+        self.px = PX(self.regions.data_ptr(), self.flags.data_ptr(), self.region.data_ptr(),
+                     self.region.data_ptr() + 4 * self.flag_off, rank, world, self.sub, 0, 0, 0)
+        torch.cuda.synchronize(device)
+        dist.barrier(group=hg.group)
+
+    def next(self):
+        """The descriptor of the next exchange (epoch + 1, the other buffer)."""
+        self.epoch += 1
+        self.px.epoch = self.epoch & 0xFFFFFFFF
+        self.px.buf_off = (self.epoch & 1) * self.world * self.sub
+        return self.px
+
+    def close(self):
+        self.mapped = []
 
 
 def kv_head_shard(num_kv_heads: int, group: Optional[dist.ProcessGroup] = None) -> HeadGroup:

@@ -11,8 +11,10 @@ process's output for its own query heads.
 * On one GPU the ranks are emulated by threads in lockstep (one CUDA stream each); their
   ``reduce`` is an element-wise torch.maximum over the ranks' blocks, which is what the
   all-reduce MAX computes.
-* On two GPUs the ranks are processes and ``reduce`` is NCCL's all-reduce MAX
-  (razorkv_b200.distributed.kv_head_shard); skipped with fewer than 2 GPUs.
+* On two GPUs the ranks are processes, exchanging either by NCCL's all-reduce MAX
+  (razorkv_b200.distributed.kv_head_shard) or by the decode kernel's stores into every rank's
+  region over NVLink with flags (``HeadGroup.enable_peer_exchange``; compactions and the
+  prefill still use the all-reduce); skipped with fewer than 2 GPUs.
 """
 
 import os
@@ -160,7 +162,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, shape, q):
+def _worker(rank, world, port, shape, peer, q):
     import torch.distributed as dist
     from datetime import timedelta
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -175,6 +177,8 @@ def _worker(rank, world, port, shape, q):
         cache = PagedRazorKVCache(_config(), LAYERS)
         cache.head_group = kv_head_shard(HKV)
         hg = cache.head_group
+        if peer:   # the exchange by peer stores over NVLink instead of the all-reduce
+            hg.enable_peer_exchange(dev, B, T + STEPS + 64)
         outs = _run(cache, shape, dev, hg.head0, hg.num_kv_heads_local)
         torch.cuda.synchronize()
         cache.check_errors()
@@ -191,14 +195,15 @@ def _worker(rank, world, port, shape, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_gpu_head_sharding_matches_one_process():
+@pytest.mark.parametrize("peer", [False, True], ids=["all_reduce", "peer_stores"])
+def test_two_gpu_head_sharding_matches_one_process(peer):
     import torch.multiprocessing as mp
     from razorkv_b200 import PagedRazorKVCache
     shape = (1, 28, 4, 128)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, shape, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, shape, peer, q)) for r in range(2)]
     for p in procs:
         p.start()
     got = sorted([q.get(timeout=600) for _ in range(2)], key=lambda x: x[0])
