@@ -722,6 +722,8 @@ def main():
     cache.check_errors()
     if world > 1:
         dist.barrier()
+        if cache.head_group is not None and cache.head_group.peer is not None:
+            cache.head_group.peer.close()   # every rank is past its last peer store
         dist.destroy_process_group()
     if rank != 0:
         return 0

@@ -368,6 +368,16 @@ typedef struct rkv_peer_exchange {
     uint32_t reserved;
 } rkv_peer_exchange;
 
+/* CUDA IPC of an exchange region between the ranks' processes.  rkv_ipc_export returns the
+ * handle (RKV_IPC_HANDLE_BYTES bytes) of the device allocation holding ptr and ptr's offset in
+ * it; rkv_ipc_import maps a peer's allocation into the CURRENT device's context (peer access
+ * enabled as needed) and returns the address of the exported pointer; rkv_ipc_release unmaps
+ * it.  Call import with the device that will run the kernels current. */
+#define RKV_IPC_HANDLE_BYTES 64
+int rkv_ipc_export(const void* ptr, void* handle, int64_t* offset);
+int rkv_ipc_import(const void* handle, int64_t offset, void** ptr);
+int rkv_ipc_release(void* ptr, int64_t offset);
+
 /* rkv_append_decode_partial with the share stored to every rank (xc gives the block layout:
  * stride_b, norm_off, head0, num_kv_heads_total; xc->x is not used).  Fused decode shapes
  * only (RKV_ERR_UNSUPPORTED otherwise; use the collective path then). */

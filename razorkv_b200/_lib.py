@@ -114,6 +114,9 @@ _SIGNATURES = {
                                                  P(Output), P(Exchange), c_vp, c_sz, c_vp]),
     "rkv_salience_apply": (ctypes.c_int, [P(KVLayout), P(Salience), P(Exchange), c_i64, c_i64,
                                           c_i64, ctypes.c_int, c_f32, c_f32, c_vp]),
+    "rkv_ipc_export": (ctypes.c_int, [c_vp, c_vp, P(c_i64)]),
+    "rkv_ipc_import": (ctypes.c_int, [c_vp, c_i64, P(c_vp)]),
+    "rkv_ipc_release": (ctypes.c_int, [c_vp, c_i64]),
     "rkv_append_decode_peer": (ctypes.c_int, [P(KVLayout), c_vp, c_vp, c_i64, c_i64, c_vp, c_vp,
                                               c_i64, ctypes.c_int, P(Query), c_f32, P(Output),
                                               P(Exchange), P(PeerExchange), c_vp, c_sz, c_vp]),

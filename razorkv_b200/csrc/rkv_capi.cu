@@ -1,6 +1,8 @@
 // C-ABI entry points of librazorkv_b200.so: argument validation, path choice, launch.
 // Every function returns an rkv_status and never allocates, frees or synchronises.
+#include <cuda.h>
 #include <math.h>
+#include <string.h>
 
 #include <atomic>
 
@@ -456,6 +458,53 @@ int rkv_append_decode_partial(const rkv_kv_layout* kv,
         return st;
     if ((st = rkv_score_partial(q, &grown, xc, stream))) return st;
     return rkv_decode_attention(q, &grown, scale, 0, out, workspace, workspace_bytes, stream);
+}
+
+// ---- CUDA IPC of an exchange region -----------------------------------------------------------
+using GetAddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+static GetAddressRangeFn address_range_fn() {
+    static GetAddressRangeFn fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return static_cast<GetAddressRangeFn>(nullptr);
+        return reinterpret_cast<GetAddressRangeFn>(p);
+    }();
+    return fn;
+}
+
+int rkv_ipc_export(const void* ptr, void* handle, int64_t* offset) {
+    if (!ptr || !handle || !offset) return RKV_ERR_INVALID_ARGUMENT;
+    GetAddressRangeFn range = address_range_fn();
+    if (!range) return RKV_ERR_CUDA;
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) return RKV_ERR_CUDA;
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)) != cudaSuccess) return RKV_ERR_CUDA;
+    static_assert(sizeof(h) == RKV_IPC_HANDLE_BYTES, "IPC handle size");
+    memcpy(handle, &h, sizeof(h));
+    *offset = (int64_t)(reinterpret_cast<CUdeviceptr>(ptr) - base);
+    return RKV_OK;
+}
+
+int rkv_ipc_import(const void* handle, int64_t offset, void** ptr) {
+    if (!handle || !ptr || offset < 0) return RKV_ERR_INVALID_ARGUMENT;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    void* base = nullptr;
+    // mapped into the current device's context, with peer access enabled as needed
+    if (cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+        return RKV_ERR_CUDA;
+    *ptr = static_cast<char*>(base) + offset;
+    return RKV_OK;
+}
+
+int rkv_ipc_release(void* ptr, int64_t offset) {
+    if (!ptr || offset < 0) return RKV_ERR_INVALID_ARGUMENT;
+    return cudaIpcCloseMemHandle(static_cast<char*>(ptr) - offset) == cudaSuccess ? RKV_OK : RKV_ERR_CUDA;
 }
 
 static int peer_status(const rkv_peer_exchange* px) {

@@ -81,10 +81,12 @@ class PeerExchange:
     """The ranks' exchange regions mapped into this process (see HeadGroup)."""
 
     def __init__(self, hg: HeadGroup, device: torch.device, batch: int, max_tokens: int):
-        from torch.multiprocessing.reductions import reduce_tensor
+        import ctypes
 
+        from . import _lib
         from ._lib import PeerExchange as PX
 
+        lib = _lib.load()
         world = dist.get_world_size(hg.group)
         rank = dist.get_rank(hg.group)
         self.world, self.rank = world, rank
@@ -95,12 +97,26 @@ class PeerExchange:
         self.region = torch.zeros(self.flag_off + 64 * ((world + 63) // 64), dtype=torch.int32,
                                   device=device)
         torch.cuda.synchronize(device)
-        rebuild, args = reduce_tensor(self.region)
-        handles = [None] * world
-        dist.all_gather_object(handles, args, group=hg.group)
-        # keep every mapped peer region alive as long as this object
-        self.mapped = [self.region if r == rank else rebuild(*handles[r]) for r in range(world)]
-        base = [t.data_ptr() for t in self.mapped]
+        handle = (ctypes.c_ubyte * 64)()
+        offset = ctypes.c_int64(0)
+        _lib.check(lib.rkv_ipc_export(self.region.data_ptr(), handle, ctypes.byref(offset)),
+                   "rkv_ipc_export")
+        shared = [None] * world
+        dist.all_gather_object(shared, (bytes(handle), offset.value), group=hg.group)
+        # map every peer's region into this rank's device context (peer access over NVLink)
+        self._imported = []
+        base = []
+        with torch.cuda.device(device):
+            for r in range(world):
+                if r == rank:
+                    base.append(self.region.data_ptr())
+                    continue
+                h = (ctypes.c_ubyte * 64).from_buffer_copy(shared[r][0])
+                ptr = ctypes.c_void_p()
+                _lib.check(lib.rkv_ipc_import(h, shared[r][1], ctypes.byref(ptr)),
+                           "rkv_ipc_import")
+                self._imported.append((ptr.value, shared[r][1]))
+                base.append(ptr.value)
         self.regions = torch.tensor(base, dtype=torch.int64, device=device)
         self.flags = torch.tensor([b + 4 * self.flag_off for b in base], dtype=torch.int64,
                                   device=device)
@@ -118,7 +134,12 @@ class PeerExchange:
         return self.px
 
     def close(self):
-        self.mapped = []
+        """Unmap the peers' regions (every rank, before the regions are freed)."""
+        from . import _lib
+        lib = _lib.load()
+        for ptr, off in self._imported:
+            lib.rkv_ipc_release(ptr, off)
+        self._imported = []
 
 
 def kv_head_shard(num_kv_heads: int, group: Optional[dist.ProcessGroup] = None) -> HeadGroup:

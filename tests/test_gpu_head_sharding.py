@@ -187,6 +187,8 @@ def _worker(rank, world, port, shape, peer, q):
                [cache.key_cache[l].cpu() for l in range(LAYERS)],
                [cache.get_cached_seq_length(l) for l in range(LAYERS)]))
         dist.barrier()
+        if peer:
+            hg.peer.close()
     except Exception as exc:
         q.put((rank, "error", repr(exc)))
         raise
@@ -194,19 +196,37 @@ def _worker(rank, world, port, shape, peer, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("peer", [False, True], ids=["all_reduce", "peer_stores"])
-def test_two_gpu_head_sharding_matches_one_process(peer):
+def _collect(procs, q, world):
+    """The workers' results; fails as soon as a worker exits without one."""
+    import queue
+    import time
+    got, deadline = [], time.monotonic() + 600
+    while len(got) < world:
+        try:
+            got.append(q.get(timeout=5))
+            continue
+        except queue.Empty:
+            pass
+        dead = [p.exitcode for p in procs if p.exitcode not in (None, 0)]
+        if dead or time.monotonic() > deadline:
+            for p in procs:
+                p.join(timeout=60)
+            pytest.fail(f"worker exit codes {[p.exitcode for p in procs]}, results {len(got)}")
+    return sorted(got, key=lambda x: x[0])
+
+
+def _spawn_and_compare(world, peer):
     import torch.multiprocessing as mp
     from razorkv_b200 import PagedRazorKVCache
     shape = (1, 28, 4, 128)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, shape, peer, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, shape, peer, q))
+             for r in range(world)]
     for p in procs:
         p.start()
-    got = sorted([q.get(timeout=600) for _ in range(2)], key=lambda x: x[0])
+    got = _collect(procs, q, world)
     for p in procs:
         p.join(timeout=120)
     for g in got:
@@ -214,6 +234,19 @@ def test_two_gpu_head_sharding_matches_one_process(peer):
     single = PagedRazorKVCache(_config(), LAYERS)
     single_outs = _run(single, shape, torch.device("cuda", 0), 0, shape[2]).cpu()
     _compare(shape, [g[1] for g in got], [g[2] for g in got], [g[3] for g in got],
-             [g[4] for g in got], [g[5] for g in got], single_outs, single, 2)
+             [g[4] for g in got], [g[5] for g in got], single_outs, single, world)
     for p in procs:
         assert p.exitcode == 0
+
+
+def test_peer_exchange_one_rank_matches_one_process():
+    """The peer-store exchange path (regions, flags, epochs, the waiting salience update) with
+    a group of one rank on one GPU: the update waits only on the flag its own preceding decode
+    launch released, so no launch waits on a concurrent one."""
+    _spawn_and_compare(1, True)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("peer", [False, True], ids=["all_reduce", "peer_stores"])
+def test_two_gpu_head_sharding_matches_one_process(peer):
+    _spawn_and_compare(2, peer)
