@@ -181,6 +181,12 @@ __device__ __forceinline__ uint16_t to_bits(float x) {
     return *reinterpret_cast<uint16_t*>(&v);
 }
 
+// Two fp32 values rounded to T and packed (lo in the low half), as to_bits on each.
+template <typename T>
+__device__ __forceinline__ uint32_t pack_bits(float lo, float hi) {
+    return (uint32_t)to_bits<T>(lo) | ((uint32_t)to_bits<T>(hi) << 16);
+}
+
 // Transpose-reduce GP per-lane partials over the 8 lanes of a group in the canonical
 // xor-4 / xor-2 / xor-1 order.  Returns the full dot of head (j >> (3 - log2 GP)).
 template <int GP>
@@ -250,19 +256,18 @@ __device__ __forceinline__ void canon_dots4(uint32_t kb, int half_bytes, const i
             qw[r][hf] = lds128(qb + (uint32_t)((hd[r] * kQRowPitch + hf * 64 + 8 * j) * 2));
         }
     }
+    const uint64_t sc2 = pack2(scale, scale);
     float part[4];
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
         uint64_t x = 0ull;   // (+0.0f, +0.0f)
 #pragma unroll
         for (int hf = 0; hf < HALVES; ++hf) {
-            uint64_t kp[4];
-            float f[8];
+            uint64_t kp[4], qp[4];
             unpack8_pairs<T>(kw[r][hf], kp);
-            unpack8<T>(qw[r][hf], f);
+            unpack8_pairs<T>(qw[r][hf], qp);
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-                ffma2(x, pack2(__fmul_rn(f[2 * i], scale), __fmul_rn(f[2 * i + 1], scale)), kp[i]);
+            for (int i = 0; i < 4; ++i) ffma2(x, fmul2(qp[i], sc2), kp[i]);
         }
         part[r] = sum_pair(x);
     }
@@ -898,6 +903,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                 // ---- 3. online softmax + P.V on tensor cores ------------------------------
                 if (a.attend) {
                     bool any_raise = false;
+                    uint32_t pb0 = 0u, pb1 = 0u;   // P.V B fragments (tensor-core logits path)
                     if constexpr (M == 0 && !SCREEN) {
                         float z[4];
                         float mx = -INFINITY;
@@ -907,15 +913,17 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                             z[r] = (t < nv && hl < G) ? sc[r] * a.logit_log2 : -INFINITY;
                             mx = fmaxf(mx, z[r]);
                         }
-                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
                         // Lazy rescaling: the running reference max only moves when the tile
                         // max exceeds it by more than 2^8, so P stays <= 256 (exact range for
                         // bf16/fp16 and fp32 sums) and the accumulator is rescaled only on
-                        // those rare tiles.
-                        const bool raise = mx > m_run + kRescaleLog2;   // includes m_run == -inf
-                        any_raise = __any_sync(0xffffffffu, raise);
+                        // those rare tiles.  A head's tile max exceeds the bound exactly when
+                        // one of its lanes' values does, so the max over the lanes is taken
+                        // only on those tiles.
+                        any_raise = __any_sync(0xffffffffu, mx > m_run + kRescaleLog2);   // includes m_run == -inf
                         if (any_raise) {
+                            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                            const bool raise = mx > m_run + kRescaleLog2;
                             const float m_new = raise ? mx : m_run;
                             const float alpha = raise ? ex2(m_run - m_new) : 1.0f;   // ex2(-inf) = 0
                             l_run *= alpha;
@@ -957,14 +965,15 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                         const float zA1 = (tB < nv && nA < G) ? c4[2] * a.attn_log2 : -INFINITY;
                         const float zB1 = (tB < nv && nB < G) ? c4[3] * a.attn_log2 : -INFINITY;
                         float mxA = fmaxf(zA0, zA1), mxB = fmaxf(zB0, zB1);
+                        // as above: the max over a head's lanes only on tiles that raise it
+                        if (__any_sync(0xffffffffu, mxA > mrA + kRescaleLog2 || mxB > mrB + kRescaleLog2)) {
 #pragma unroll
-                        for (int o = 4; o < 32; o <<= 1) {
-                            mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, o));
-                            mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, o));
-                        }
-                        const bool raiseA = mxA > mrA + kRescaleLog2;   // includes mr == -inf
-                        const bool raiseB = mxB > mrB + kRescaleLog2;
-                        if (__any_sync(0xffffffffu, raiseA || raiseB)) {
+                            for (int o = 4; o < 32; o <<= 1) {
+                                mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, o));
+                                mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, o));
+                            }
+                            const bool raiseA = mxA > mrA + kRescaleLog2;   // includes mr == -inf
+                            const bool raiseB = mxB > mrB + kRescaleLog2;
                             const float alA = raiseA ? ex2(mrA - mxA) : 1.0f;   // ex2(-inf) = 0
                             const float alB = raiseB ? ex2(mrB - mxB) : 1.0f;
                             if (raiseA) { lrA *= alA; mrA = mxA; }
@@ -982,10 +991,13 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                         const float pB1 = liveB ? ex2(zB1 - mrB) : 0.0f;
                         lrA += pA0 + pA1;
                         lrB += pB0 + pB1;
-                        sm.ps[warp][nA][tA] = to_bits<T>(pA0);
-                        sm.ps[warp][nB][tA] = to_bits<T>(pB0);
-                        sm.ps[warp][nA][tB] = to_bits<T>(pA1);
-                        sm.ps[warp][nB][tB] = to_bits<T>(pB1);
+                        // P as the P.V mma's B fragments without a trip through shared
+                        // memory: the lane's (token, head pair) in the accumulator layout is
+                        // one element pair of an 8x8 row-major fragment (tokens 0-7 and 8-15),
+                        // and the transposed fragment is exactly B's layout (tokens
+                        // 2(lane%4) + {0,1} (+8), head lane/4)
+                        pb0 = movmatrix_trans(pack_bits<T>(pA0, pB0));
+                        pb1 = movmatrix_trans(pack_bits<T>(pA1, pB1));
                     }
                     if (nv < kTileTokens) {
                         // zero V rows past the last valid token (their P is 0; keep them finite)
@@ -1007,8 +1019,11 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                             acc[mt][2] *= al0; acc[mt][3] *= al1;
                         }
                     }
-                    const uint32_t b0 = lds32(ps_base + ((lane >> 2) * kTileTokens + n0) * 2);
-                    const uint32_t b1 = lds32(ps_base + ((lane >> 2) * kTileTokens + n0 + 8) * 2);
+                    uint32_t b0 = pb0, b1 = pb1;
+                    if constexpr (M == 0 && !SCREEN) {
+                        b0 = lds32(ps_base + ((lane >> 2) * kTileTokens + n0) * 2);
+                        b1 = lds32(ps_base + ((lane >> 2) * kTileTokens + n0 + 8) * 2);
+                    }
                     const int mi = lane >> 3;
                     const int tk = (mi >> 1) * 8 + (lane & 7);
 #pragma unroll

@@ -166,6 +166,14 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a
     }
 }
 
+// Transpose of an 8x8 16-bit matrix held one element pair per lane (lane l: row l/4,
+// columns 2(l%4) and 2(l%4) + 1); the result has the same layout.
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+
 // Packed fp32 pairs (low word = first element) and the paired FMA of sm_100a: both halves are
 // independent IEEE fma.rn operations.
 __device__ __forceinline__ uint64_t pack2(float lo, float hi) {
@@ -176,6 +184,13 @@ __device__ __forceinline__ uint64_t pack2(float lo, float hi) {
 
 __device__ __forceinline__ void ffma2(uint64_t& acc, uint64_t a, uint64_t b) {
     asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(b));
+}
+
+// Both halves multiplied, each an IEEE mul.rn (as __fmul_rn).
+__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
 }
 
 // low + high half, rounded once (the canonical even + odd combination)
