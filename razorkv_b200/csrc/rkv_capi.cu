@@ -29,14 +29,13 @@ inline int status_of(cudaError_t e) {
 
 inline bool dtype_ok(int d) { return d == RKV_F32 || d == RKV_F16 || d == RKV_BF16; }
 
-// Workspace layout: [0, 4) error flag, [256, header) per-sequence merge counters (int32),
-// [header, ...) scratch of the call.
+// Workspace layout: [0, 4) error flag, [256, header) cross-CTA counters (int32; every launch
+// leaves them at zero), [header, ...) scratch of the call.
 inline int* ws_err(void* ws) { return static_cast<int*>(ws); }
 inline int* ws_counters(void* ws) { return reinterpret_cast<int*>(static_cast<char*>(ws) + 256); }
 inline float* ws_body(void* ws) {
     return reinterpret_cast<float*>(static_cast<char*>(ws) + RKV_WORKSPACE_HEADER_BYTES);
 }
-constexpr int64_t kMaxCounters = (RKV_WORKSPACE_HEADER_BYTES - 256) / 4;
 
 int check_kv(const rkv_kv_layout* kv, bool need_v) {
     if (!kv || !kv->k || (need_v && !kv->v)) return RKV_ERR_INVALID_ARGUMENT;

@@ -633,22 +633,24 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
         const int64_t seg_end = min(r1, (b + 1) * a.n_tiles);
         const int64_t tb0 = pos - b * a.n_tiles, tb1 = seg_end - b * a.n_tiles;
 
-        if constexpr (SCREEN) {
-            // B fragments of the score query q (MODE 2) and of the magnitudes of whichever
-            // query scores (q in both modes: in MODE 0 the attention query is q itself)
+        if constexpr (M != 0) {
+            // B = q2^T (dims x heads): lane holds head lane/4, dims 16kk + 2(lane%4) + {0,1}
+            // (b0) and the same + 8 (b1); heads past G are zero.  Issued first: in the
+            // screened instances these loads overlap the staging of the scoring rows below.
             const int n = lane >> 2;
-            const T* qr = static_cast<const T*>(a.q) + b * a.q_stride_b + (int64_t)(h * G + n) * a.q_stride_h;
+            const T* qr = static_cast<const T*>(a.q2) + b * a.q2_stride_b + (int64_t)(h * G + n) * a.q2_stride_h;
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk) {
                 const int d0 = kk * 16 + 2 * (lane & 3);
-                const uint32_t f0 = n < G ? pack_elems<T>(qr[d0], qr[d0 + 1]) : 0u;
-                const uint32_t f1 = n < G ? pack_elems<T>(qr[d0 + 8], qr[d0 + 9]) : 0u;
-                if constexpr (M == 2) { qsf[kk][0] = f0; qsf[kk][1] = f1; }
-                qa[kk][0] = f0 & kAbsMask2;
-                qa[kk][1] = f1 & kAbsMask2;
+                qf[kk][0] = n < G ? pack_elems<T>(qr[d0], qr[d0 + 1]) : 0u;
+                qf[kk][1] = n < G ? pack_elems<T>(qr[d0 + 8], qr[d0 + 9]) : 0u;
             }
-            // this warp's copy of the G scoring-query rows for the canonical recompute
-            // (16-byte rows; the host requires 16-byte aligned query rows for these instances)
+        }
+        if constexpr (SCREEN) {
+            // this warp's copy of the G scoring-query rows (q) for the canonical recompute
+            // (16-byte rows; the host requires 16-byte aligned query rows for these
+            // instances), then every fragment of q from the copy: one round trip to global
+            // memory per segment instead of one per fragment set
             __syncwarp();   // the previous segment's reads of the copy are done
             const T* qg = static_cast<const T*>(a.q) + b * a.q_stride_b + (int64_t)(h * G) * a.q_stride_h;
             for (int idx = lane; idx < G * (D / 8); idx += 32) {
@@ -657,6 +659,23 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                 sts128(smem_u32(&qrows.q[warp][i][c8 * 8]), w);
             }
             __syncwarp();
+            // B fragments of q (the attention query too in MODE 0, the score query in MODE 2)
+            // and of its magnitudes; heads past G are zero
+            const int n = lane >> 2;
+            const uint32_t qrow = smem_u32(&qrows.q[warp][n < G ? n : 0][0]);
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+                const int d0 = kk * 16 + 2 * (lane & 3);
+                const uint32_t f0 = n < G ? lds32(qrow + d0 * 2) : 0u;
+                const uint32_t f1 = n < G ? lds32(qrow + (d0 + 8) * 2) : 0u;
+                if constexpr (M == 2) {
+                    qsf[kk][0] = f0; qsf[kk][1] = f1;
+                } else {
+                    qf[kk][0] = f0; qf[kk][1] = f1;
+                }
+                qa[kk][0] = f0 & kAbsMask2;
+                qa[kk][1] = f1 & kAbsMask2;
+            }
         }
         if constexpr (M != 1 && !SCREEN) {
             // fl(q * scale) for this lane's K elements: chunk j of every 64-element half
@@ -671,18 +690,6 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                     const float hi = i < G ? __fmul_rn(to_f<T>(qr[1]), a.scale_r) : 0.0f;
                     qreg[i][e / 2] = pack2(lo, hi);
                 }
-            }
-        }
-        if constexpr (M != 0 || SCREEN) {
-            // B = q2^T (dims x heads): lane holds head lane/4, dims 16kk + 2(lane%4) + {0,1}
-            // (b0) and the same + 8 (b1); heads past G are zero.  (q2 is q in MODE 0.)
-            const int n = lane >> 2;
-            const T* qr = static_cast<const T*>(a.q2) + b * a.q2_stride_b + (int64_t)(h * G + n) * a.q2_stride_h;
-#pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk) {
-                const int d0 = kk * 16 + 2 * (lane & 3);
-                qf[kk][0] = n < G ? pack_elems<T>(qr[d0], qr[d0 + 1]) : 0u;
-                qf[kk][1] = n < G ? pack_elems<T>(qr[d0 + 8], qr[d0 + 9]) : 0u;
             }
         }
         float m_run = -INFINITY, l_run = 0.0f;   // MODE 0: running max / sum of head hl

@@ -11,19 +11,18 @@
 // RKV_NOALLOC_SCRATCH_BYTES of it until the process exits.  Host code cannot use the array's
 // name as a device address (on the host it names a host-side stand-in), so the first call on
 // each device looks up the real device address with cudaGetSymbolAddress while that device is
-// current and keeps it; make that first call before any stream capture.  The array is shared
-// by every call on the device and keeps the previous call's contents, so each valid call
-// clears, on its stream and before its launch, the part that must start at zero: the error
-// flag word and the merge counters of its batch.  That clear is a small memset between two
-// decode launches, so consecutive calls do not overlap a launch's start with the previous
-// one's tail as rkv_decode_attention with a caller workspace does.  Calls whose kernels
-// overlap on the GPU (different streams, or different host threads) race on the array;
-// serialise them.
+// current and keeps it; make that first call before any stream capture.  The array starts
+// at zero like every device variable, and the decode kernels leave the cross-CTA counters in
+// its header at zero when they finish, so nothing is cleared between calls and consecutive
+// calls overlap a launch's start with the previous one's tail exactly as
+// rkv_decode_attention with a caller workspace does.  The array is shared by every call on
+// the device: calls whose kernels overlap on the GPU (different streams, or different host
+// threads) race on it; serialise them.
 //
 // Device-side errors are not reported here.  The decode kernels record a bounded wait that
 // gave up, or a page id outside the storage, in the error flag inside the scratch array,
-// which no entry point reads back, and the next call clears it.  A caller that needs those
-// errors uses rkv_decode_attention with a workspace it can read (its first int32, at
+// which no entry point reads back.  A caller that needs those errors uses
+// rkv_decode_attention with a workspace it can read (its first int32, at
 // rkv_workspace_error_flag_offset()).
 #include <cuda_runtime.h>
 
@@ -71,11 +70,6 @@ extern "C" int rkv_decode_attention_noalloc(const rkv_query* q, const rkv_kv_lay
     void* ws = nullptr;
     st = scratch_address(&ws);
     if (st) return st;
-    // error flag [0, 4) and the per-sequence merge counters [256, 256 + 4 B) of the header
-    const size_t clear = 256 + 4 * (size_t)kv->batch;
-    if (cudaMemsetAsync(ws, 0, clear < RKV_WORKSPACE_HEADER_BYTES ? clear : RKV_WORKSPACE_HEADER_BYTES,
-                        static_cast<cudaStream_t>(stream)) != cudaSuccess)
-        return RKV_ERR_CUDA;
     return rkv_decode_attention(q, kv, scale, causal, out, ws, (size_t)RKV_NOALLOC_SCRATCH_BYTES,
                                 stream);
 }
