@@ -618,6 +618,8 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
     const int G = a.G;
     const bool head_writer = (j & ((8 / GP) - 1)) == 0;   // one lane per head in each group
     const uint32_t ps_base = smem_u32(&sm.ps[warp][0][0]);
+    const bool qvec = !(reinterpret_cast<uintptr_t>(a.q) & 15) && !((a.q_stride_h * 2) & 15) &&
+                      !((a.q_stride_b * 2) & 15);
 
     // MODE 0 / 2 without the screen: fl(q * scale) as (even, odd) element pairs
     uint64_t qreg[SCREEN ? 1 : GP][EPL / 2];
@@ -679,17 +681,48 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
         }
         if constexpr (M != 1 && !SCREEN) {
             // fl(q * scale) for this lane's K elements: chunk j of every 64-element half
+            // (one 16-byte load per chunk when the query rows are 16-byte aligned)
             const T* qb = static_cast<const T*>(a.q) + b * a.q_stride_b;
+            if (qvec) {
 #pragma unroll
-            for (int i = 0; i < GP; ++i) {
+                for (int i = 0; i < GP; ++i) {
 #pragma unroll
-                for (int e = 0; e < EPL; e += 2) {
-                    const int dim = (e / 8) * 64 + 8 * j + (e % 8);
-                    const T* qr = qb + (int64_t)(h * G + i) * a.q_stride_h + dim;
-                    const float lo = i < G ? __fmul_rn(to_f<T>(qr[0]), a.scale_r) : 0.0f;
-                    const float hi = i < G ? __fmul_rn(to_f<T>(qr[1]), a.scale_r) : 0.0f;
-                    qreg[i][e / 2] = pack2(lo, hi);
+                    for (int hf = 0; hf < HALVES; ++hf) {
+                        float f[8];
+                        const uint4 w = i < G ? *reinterpret_cast<const uint4*>(
+                                                    qb + (int64_t)(h * G + i) * a.q_stride_h + hf * 64 + 8 * j)
+                                              : make_uint4(0u, 0u, 0u, 0u);
+                        unpack8<T>(w, f);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            qreg[i][hf * 4 + e] = pack2(__fmul_rn(f[2 * e], a.scale_r),
+                                                        __fmul_rn(f[2 * e + 1], a.scale_r));
+                    }
                 }
+            } else {
+#pragma unroll
+                for (int i = 0; i < GP; ++i) {
+#pragma unroll
+                    for (int e = 0; e < EPL; e += 2) {
+                        const int dim = (e / 8) * 64 + 8 * j + (e % 8);
+                        const T* qr = qb + (int64_t)(h * G + i) * a.q_stride_h + dim;
+                        const float lo = i < G ? __fmul_rn(to_f<T>(qr[0]), a.scale_r) : 0.0f;
+                        const float hi = i < G ? __fmul_rn(to_f<T>(qr[1]), a.scale_r) : 0.0f;
+                        qreg[i][e / 2] = pack2(lo, hi);
+                    }
+                }
+            }
+        }
+        if (seg_end < r1 && lane < 2 * G) {
+            // the next segment's query rows of this warp's heads into L2 (two 128-byte lines
+            // per row at most), so its setup above does not wait on DRAM
+            const int64_t qo = (b + 1) * a.q_stride_b + (int64_t)(h * G + (lane >> 1)) * a.q_stride_h +
+                               (lane & 1) * 64;
+            if ((lane & 1) == 0 || D > 64) prefetch_l2(static_cast<const T*>(a.q) + qo);
+            if constexpr (M != 0) {
+                const int64_t q2o = (b + 1) * a.q2_stride_b +
+                                    (int64_t)(h * G + (lane >> 1)) * a.q2_stride_h + (lane & 1) * 64;
+                if ((lane & 1) == 0 || D > 64) prefetch_l2(static_cast<const T*>(a.q2) + q2o);
             }
         }
         float m_run = -INFINITY, l_run = 0.0f;   // MODE 0: running max / sum of head hl

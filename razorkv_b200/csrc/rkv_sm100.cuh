@@ -237,6 +237,11 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
     return v;
 }
 
+// Brings the 128-byte line holding p into L2 (a hint; no completion).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 // Named barrier over the compute warps only (the producer warp never joins it).
 __device__ __forceinline__ void compute_barrier(int nthreads) {
     asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
