@@ -64,7 +64,10 @@ constexpr int kQRowPitch = 128;           // elements between the query rows sta
 struct DevArgs {
     const void* q; int64_t q_stride_b, q_stride_h;
     int Hq, Hkv, G, wph;
-    int64_t B, N, n_tiles, total, W, maxc;
+    // stream-K positions: sequence b owns positions [b * seq_pos, (b + 1) * seq_pos); the
+    // first lead of them are empty (they stand for the fixed cost of starting a sequence in a
+    // CTA), tile t of b sits at b * seq_pos + lead + t
+    int64_t B, N, n_tiles, total, W, maxc, seq_pos, lead;
     const int64_t* pt; int64_t pt_stride_b; int64_t num_slots;
     float* sal; int64_t sal_stride_b, sal_stride_p;
     float scale_r, logit_log2, decay, omd;
@@ -347,9 +350,9 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
         prefetch_tensormap(&tmk);
         if (a.attend) prefetch_tensormap(&tmv);
         if (r0 < r1) {
-            const int64_t b = r0 / a.n_tiles;
-            const int64_t t_begin = r0 - b * a.n_tiles;
-            const int64_t t_seg = min(r1, (b + 1) * a.n_tiles) - b * a.n_tiles;
+            const int64_t b = r0 / a.seq_pos;
+            const int64_t t_begin = max(r0 - b * a.seq_pos - a.lead, (int64_t)0);
+            const int64_t t_seg = max(min(r1, (b + 1) * a.seq_pos) - b * a.seq_pos - a.lead, (int64_t)0);
             const int64_t t_end = min(t_seg, t_begin + (int64_t)wph);
             for (int64_t t = t_begin; t < t_end; ++t) {
                 const int64_t v = __ldcg(a.pt + b * a.pt_stride_b + t);
@@ -393,9 +396,10 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
             int slot = 0;
             uint32_t par = 0;
             for (int64_t pos = r0; pos < r1;) {
-                const int64_t b = pos / a.n_tiles;
-                const int64_t seg_end = min(r1, (b + 1) * a.n_tiles);
-                const int64_t tb0 = pos - b * a.n_tiles, tb1 = seg_end - b * a.n_tiles;
+                const int64_t b = pos / a.seq_pos;
+                const int64_t seg_end = min(r1, (b + 1) * a.seq_pos);
+                const int64_t tb0 = max(pos - b * a.seq_pos - a.lead, (int64_t)0);
+                const int64_t tb1 = max(seg_end - b * a.seq_pos - a.lead, (int64_t)0);
                 for (int64_t t0 = tb0; t0 < tb1; t0 += wph) {
                     const int ntile = (int)(tb1 - t0 < wph ? tb1 - t0 : wph);
                     if constexpr (POOL) {
@@ -544,9 +548,10 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
         int slot = 0;
         uint32_t par = 0;
         for (int64_t pos = r0; pos < r1;) {
-            const int64_t b = pos / a.n_tiles;
-            const int64_t seg_end = min(r1, (b + 1) * a.n_tiles);
-            const int64_t tb0 = pos - b * a.n_tiles, tb1 = seg_end - b * a.n_tiles;
+            const int64_t b = pos / a.seq_pos;
+            const int64_t seg_end = min(r1, (b + 1) * a.seq_pos);
+            const int64_t tb0 = max(pos - b * a.seq_pos - a.lead, (int64_t)0);
+            const int64_t tb1 = max(seg_end - b * a.seq_pos - a.lead, (int64_t)0);
             const int64_t* ptb = a.pt + b * a.pt_stride_b;
             int64_t win = tb0;   // first tile of the page-id window held in registers
             int64_t pid = (win + lane < tb1) ? __ldg(ptb + win + lane) : 0;
@@ -631,9 +636,10 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
     int slot = 0;
     uint32_t par = 0;
     for (int64_t pos = r0; pos < r1;) {
-        const int64_t b = pos / a.n_tiles;
-        const int64_t seg_end = min(r1, (b + 1) * a.n_tiles);
-        const int64_t tb0 = pos - b * a.n_tiles, tb1 = seg_end - b * a.n_tiles;
+        const int64_t b = pos / a.seq_pos;
+        const int64_t seg_end = min(r1, (b + 1) * a.seq_pos);
+        const int64_t tb0 = max(pos - b * a.seq_pos - a.lead, (int64_t)0);
+        const int64_t tb1 = max(seg_end - b * a.seq_pos - a.lead, (int64_t)0);
 
         if constexpr (M != 0) {
             // B = q2^T (dims x heads): lane holds head lane/4, dims 16kk + 2(lane%4) + {0,1}
@@ -711,18 +717,6 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                         qreg[i][e / 2] = pack2(lo, hi);
                     }
                 }
-            }
-        }
-        if (seg_end < r1 && lane < 2 * G) {
-            // the next segment's query rows of this warp's heads into L2 (two 128-byte lines
-            // per row at most), so its setup above does not wait on DRAM
-            const int64_t qo = (b + 1) * a.q_stride_b + (int64_t)(h * G + (lane >> 1)) * a.q_stride_h +
-                               (lane & 1) * 64;
-            if ((lane & 1) == 0 || D > 64) prefetch_l2(static_cast<const T*>(a.q) + qo);
-            if constexpr (M != 0) {
-                const int64_t q2o = (b + 1) * a.q2_stride_b +
-                                    (int64_t)(h * G + (lane >> 1)) * a.q2_stride_h + (lane & 1) * 64;
-                if ((lane & 1) == 0 || D > 64) prefetch_l2(static_cast<const T*>(a.q2) + q2o);
             }
         }
         float m_run = -INFINITY, l_run = 0.0f;   // MODE 0: running max / sum of head hl
@@ -1089,7 +1083,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
         // merge_kernel combines the partials of a sequence once the whole grid is done
         if (a.attend) {
             constexpr int RS = D + 4;
-            const int64_t cfirst = (b * a.n_tiles) / a.W;
+            const int64_t cfirst = (b * a.seq_pos) / a.W;
             const int64_t pidx = (c - cfirst) * wph + s;
             float* part = a.partials + ((b * a.maxc * wph + pidx) * a.Hq) * (int64_t)RS;
             if constexpr (M == 0 && !SCREEN) {
@@ -1151,7 +1145,7 @@ constexpr int kMergePartialsPerCta = 40;   // cluster size: ceil(partials / 40),
 
 struct MergeArgs {
     const float* partials; void* out; int64_t o_stride_b, o_stride_h;
-    int Hq, wph; int64_t n_tiles, W, maxc;
+    int Hq, wph; int64_t seq_pos, W, maxc;   // stream-K positions per sequence (DevArgs)
     int cluster;   // CTAs per row (the launch's cluster size)
 };
 
@@ -1170,8 +1164,8 @@ merge_kernel(const MergeArgs a) {
     const int d = threadIdx.x % D;
     const int64_t b = blockIdx.x / a.Hq;
     const int hq = blockIdx.x % a.Hq;
-    const int64_t cfirst = (b * a.n_tiles) / a.W;
-    const int64_t clast = ((b + 1) * a.n_tiles - 1) / a.W;
+    const int64_t cfirst = (b * a.seq_pos) / a.W;
+    const int64_t clast = ((b + 1) * a.seq_pos - 1) / a.W;
     const int np = (int)(clast - cfirst + 1) * a.wph;
     // group g takes whole 32-partial chunks g, g + G, g + 2G, ...
     const float* pb = a.partials + ((b * a.maxc * a.wph) * a.Hq + hq) * (int64_t)RS;
@@ -1243,8 +1237,8 @@ merge_cluster_kernel(const MergeArgs a) {
     const int row = (int)(blockIdx.x / (unsigned)S);
     const int64_t b = row / a.Hq;
     const int hq = row % a.Hq;
-    const int64_t cfirst = (b * a.n_tiles) / a.W;
-    const int64_t clast = ((b + 1) * a.n_tiles - 1) / a.W;
+    const int64_t cfirst = (b * a.seq_pos) / a.W;
+    const int64_t clast = ((b + 1) * a.seq_pos - 1) / a.W;
     const int np = (int)(clast - cfirst + 1) * a.wph;
     // this CTA's share of the row; group g takes its 32-partial chunks g, g + G, ...
     const int lo = np * rank / S, hi = np * (rank + 1) / S;
@@ -1370,20 +1364,27 @@ __global__ void __launch_bounds__(64) wait_timeout_kernel(int* result, long long
 }
 
 struct Plan {
-    int64_t n_tiles, total, W, grid, maxc;
+    int64_t n_tiles, seq_pos, lead, total, W, grid, maxc;
     int wph, stages, stage_bytes, tile_bytes, kv_tile_bytes, half_bytes, smem_bytes;
 };
 
 static Plan make_plan(int64_t B, int64_t N, int Hkv, int D, bool attend) {
     Plan p{};
     p.n_tiles = (N + kTileTokens - 1) / kTileTokens;
-    p.total = B * p.n_tiles;
+    p.wph = kComputeWarps / Hkv;
+    // A CTA whose range crosses from one sequence to the next pays ~3-4.5 us more than the
+    // others (the appended token at the first sequence's end, its partials out, the next
+    // query in): a per-CTA timeline put those CTAs last in every launch.  Three stages of
+    // empty positions before every sequence give them that much less real work, so they
+    // finish with the rest (with one sequence no range crosses a boundary).
+    p.lead = B > 1 ? 3 * p.wph : 0;
+    p.seq_pos = p.n_tiles + p.lead;
+    p.total = B * p.seq_pos;
     const int64_t sms = num_sms();
     const int64_t grid0 = p.total < sms ? p.total : sms;
     p.W = grid0 > 0 ? (p.total + grid0 - 1) / grid0 : 1;
     p.grid = p.W > 0 ? (p.total + p.W - 1) / p.W : 0;
-    p.maxc = p.n_tiles / p.W + 2;
-    p.wph = kComputeWarps / Hkv;
+    p.maxc = p.seq_pos / p.W + 2;
     p.half_bytes = Hkv * kTileTokens * 128;
     p.kv_tile_bytes = (D / 64) * p.half_bytes;
     p.tile_bytes = (attend ? 2 : 1) * p.kv_tile_bytes;
@@ -1477,6 +1478,7 @@ static cudaError_t launch_t(const FusedParams& f, const Plan& pl, CUtensorMapDat
     a.q = f.q; a.q_stride_b = f.q_stride_b; a.q_stride_h = f.q_stride_h;
     a.Hq = f.Hq; a.Hkv = f.Hkv; a.G = f.Hq / f.Hkv; a.wph = pl.wph;
     a.B = f.B; a.N = f.N; a.n_tiles = pl.n_tiles; a.total = pl.total; a.W = pl.W; a.maxc = pl.maxc;
+    a.seq_pos = pl.seq_pos; a.lead = pl.lead;
     a.pt = f.page_table; a.pt_stride_b = f.pt_stride_b; a.num_slots = f.num_slots;
     a.sal = f.sal; a.sal_stride_b = f.sal_stride_b; a.sal_stride_p = f.sal_stride_p;
     a.scale_r = f.scale_r; a.logit_log2 = f.logit_mul * 1.4426950408889634f;
@@ -1522,7 +1524,7 @@ static cudaError_t launch_t(const FusedParams& f, const Plan& pl, CUtensorMapDat
     const int64_t np_max = pl.maxc * pl.wph;
     int S = (int)((np_max + kMergePartialsPerCta - 1) / kMergePartialsPerCta);
     S = S < 1 ? 1 : S > kMergeMaxCluster ? kMergeMaxCluster : S;
-    MergeArgs m{f.partials, f.out, f.o_stride_b, f.o_stride_h, f.Hq, pl.wph, pl.n_tiles, pl.W,
+    MergeArgs m{f.partials, f.out, f.o_stride_b, f.o_stride_h, f.Hq, pl.wph, pl.seq_pos, pl.W,
                 pl.maxc, S};
     cudaLaunchAttribute mattr[2];
     mattr[0] = attr[0];
