@@ -89,10 +89,13 @@ def peaks():
 class ClockSampler:
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap,uuid")
 
-    def __init__(self, gpu_index):
+    def __init__(self, gpu_index, uuid=None):
+        # nvidia-smi lists the GPUs by their index on the machine, whatever CUDA_VISIBLE_DEVICES
+        # says, so this process's GPU is found by its UUID (by index only when that is unknown)
         self.gpu = gpu_index
+        self.uuid = str(uuid).lower().removeprefix("gpu-") if uuid else None
         self.proc = None
         self.path = os.path.join(tempfile.gettempdir(), f"rkv_clocks_{os.getpid()}_{gpu_index}.csv")
 
@@ -123,7 +126,12 @@ class ClockSampler:
             pass
         for line in lines:
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9 or not parts[0].isdigit() or int(parts[0]) != self.gpu:
+            if len(parts) < 10 or not parts[0].isdigit():
+                continue
+            if self.uuid is not None:
+                if parts[9].lower().removeprefix("gpu-") != self.uuid:
+                    continue
+            elif int(parts[0]) != self.gpu:
                 continue
             try:
                 sm.append(float(parts[1]))
@@ -597,7 +605,11 @@ def main():
     lib = _lib.load()
     # every rank samples its own GPU's clocks; the samplers start before the barrier so that
     # no rank enters the timed region while another is still setting up
-    clocks = ClockSampler(local)
+    try:
+        gpu_uuid = torch.cuda.get_device_properties(dev).uuid
+    except Exception:   # noqa: BLE001 - fall back to the index
+        gpu_uuid = None
+    clocks = ClockSampler(local, gpu_uuid)
     clocks.start()
     time.sleep(0.4)
     timer.prepare(-(-args.steps // timer.every) * len(layers) + 8)
