@@ -68,6 +68,9 @@ struct DevArgs {
     // first lead of them are empty (they stand for the fixed cost of starting a sequence in a
     // CTA), tile t of b sits at b * seq_pos + lead + t
     int64_t B, N, n_tiles, total, W, maxc, seq_pos, lead;
+    // partials per CTA and row: wph, or 1 when the tile slots' partials are folded inside
+    // the CTA first (one-sequence launches of the tensor-core-logit instances)
+    int pw;
     const int64_t* pt; int64_t pt_stride_b; int64_t num_slots;
     float* sal; int64_t sal_stride_b, sal_stride_p;
     float scale_r, logit_log2, decay, omd;
@@ -1081,10 +1084,58 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
         // ---- segment end: write this warp's partial --------------------------------------
         // partial row per query head: acc[0, D) | m (log2 units) at D | l at D+1 | pad;
         // merge_kernel combines the partials of a sequence once the whole grid is done
-        if (a.attend) {
+        bool writer = true;
+        if constexpr (SCREEN || M != 0) {
+            if (a.attend && a.pw == 1 && wph > 1) {
+                // One-sequence launch: fold the tile slots' partials of each kv head here (the
+                // merge then reads one partial per CTA).  Once every compute warp is past its
+                // last tile the stage ring is idle (the CTA's only segment is done and every
+                // copy has landed); warps of slot s >= 1 publish their state there, slot 0
+                // folds it in the accumulator layout, which is the same for every warp of a
+                // kv head.
+                constexpr int SW = MT * 4 + 4;   // floats a lane publishes
+                float* pub = reinterpret_cast<float*>(smem);
+                compute_barrier(kComputeThreads);   // every warp is done reading the stages
+                if (s > 0) {
+                    float* my = pub + ((warp - Hkv) * 32 + lane) * SW;
+#pragma unroll
+                    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) my[mt * 4 + e] = acc[mt][e];
+                    my[MT * 4 + 0] = mrA; my[MT * 4 + 1] = mrB;
+                    my[MT * 4 + 2] = lrA; my[MT * 4 + 3] = lrB;
+                }
+                compute_barrier(kComputeThreads);
+                if (s == 0) {
+                    for (int so = 1; so < wph; ++so) {
+                        const float* ot = pub + ((so * Hkv + h - Hkv) * 32 + lane) * SW;
+                        const float moA = ot[MT * 4 + 0], moB = ot[MT * 4 + 1];
+                        const float mnA = fmaxf(mrA, moA), mnB = fmaxf(mrB, moB);
+                        // weights 2^(m - max); a side that saw no token weighs 0
+                        const float wsA = mrA == -INFINITY ? 0.f : ex2(mrA - mnA);
+                        const float woA = moA == -INFINITY ? 0.f : ex2(moA - mnA);
+                        const float wsB = mrB == -INFINITY ? 0.f : ex2(mrB - mnB);
+                        const float woB = moB == -INFINITY ? 0.f : ex2(moB - mnB);
+#pragma unroll
+                        for (int mt = 0; mt < MT; ++mt) {
+                            acc[mt][0] = acc[mt][0] * wsA + ot[mt * 4 + 0] * woA;
+                            acc[mt][1] = acc[mt][1] * wsB + ot[mt * 4 + 1] * woB;
+                            acc[mt][2] = acc[mt][2] * wsA + ot[mt * 4 + 2] * woA;
+                            acc[mt][3] = acc[mt][3] * wsB + ot[mt * 4 + 3] * woB;
+                        }
+                        lrA = lrA * wsA + ot[MT * 4 + 2] * woA;
+                        lrB = lrB * wsB + ot[MT * 4 + 3] * woB;
+                        mrA = mnA;
+                        mrB = mnB;
+                    }
+                }
+                writer = s == 0;
+            }
+        }
+        if (a.attend && writer) {
             constexpr int RS = D + 4;
             const int64_t cfirst = (b * a.seq_pos) / a.W;
-            const int64_t pidx = (c - cfirst) * wph + s;
+            const int64_t pidx = (c - cfirst) * a.pw + s;
             float* part = a.partials + ((b * a.maxc * wph + pidx) * a.Hq) * (int64_t)RS;
             if constexpr (M == 0 && !SCREEN) {
                 float l_tot = l_run + __shfl_xor_sync(0xffffffffu, l_run, 8);
@@ -1146,6 +1197,7 @@ constexpr int kMergePartialsPerCta = 40;   // cluster size: ceil(partials / 40),
 struct MergeArgs {
     const float* partials; void* out; int64_t o_stride_b, o_stride_h;
     int Hq, wph; int64_t seq_pos, W, maxc;   // stream-K positions per sequence (DevArgs)
+    int pw;        // partials per CTA and row (DevArgs)
     int cluster;   // CTAs per row (the launch's cluster size)
 };
 
@@ -1166,7 +1218,7 @@ merge_kernel(const MergeArgs a) {
     const int hq = blockIdx.x % a.Hq;
     const int64_t cfirst = (b * a.seq_pos) / a.W;
     const int64_t clast = ((b + 1) * a.seq_pos - 1) / a.W;
-    const int np = (int)(clast - cfirst + 1) * a.wph;
+    const int np = (int)(clast - cfirst + 1) * a.pw;
     // group g takes whole 32-partial chunks g, g + G, g + 2G, ...
     const float* pb = a.partials + ((b * a.maxc * a.wph) * a.Hq + hq) * (int64_t)RS;
     const int64_t pstride = (int64_t)a.Hq * RS;
@@ -1239,7 +1291,7 @@ merge_cluster_kernel(const MergeArgs a) {
     const int hq = row % a.Hq;
     const int64_t cfirst = (b * a.seq_pos) / a.W;
     const int64_t clast = ((b + 1) * a.seq_pos - 1) / a.W;
-    const int np = (int)(clast - cfirst + 1) * a.wph;
+    const int np = (int)(clast - cfirst + 1) * a.pw;
     // this CTA's share of the row; group g takes its 32-partial chunks g, g + G, ...
     const int lo = np * rank / S, hi = np * (rank + 1) / S;
     const float* pb = a.partials + ((b * a.maxc * a.wph) * a.Hq + hq) * (int64_t)RS;
@@ -1479,6 +1531,10 @@ static cudaError_t launch_t(const FusedParams& f, const Plan& pl, CUtensorMapDat
     a.Hq = f.Hq; a.Hkv = f.Hkv; a.G = f.Hq / f.Hkv; a.wph = pl.wph;
     a.B = f.B; a.N = f.N; a.n_tiles = pl.n_tiles; a.total = pl.total; a.W = pl.W; a.maxc = pl.maxc;
     a.seq_pos = pl.seq_pos; a.lead = pl.lead;
+    // one-sequence launches of the instances with tensor-core logits fold their tile slots'
+    // partials inside the CTA (one partial per CTA and row for the merge)
+    constexpr bool kMmaLayout = GP == 8 || MODE == 1 || MODE == 2;
+    a.pw = (kMmaLayout && f.B == 1 && pl.wph > 1 && f.attend) ? 1 : pl.wph;
     a.pt = f.page_table; a.pt_stride_b = f.pt_stride_b; a.num_slots = f.num_slots;
     a.sal = f.sal; a.sal_stride_b = f.sal_stride_b; a.sal_stride_p = f.sal_stride_p;
     a.scale_r = f.scale_r; a.logit_log2 = f.logit_mul * 1.4426950408889634f;
@@ -1521,11 +1577,11 @@ static cudaError_t launch_t(const FusedParams& f, const Plan& pl, CUtensorMapDat
     if (e != cudaSuccess || !f.attend) return e;
     // CTAs per row: enough that each folds ~kMergePartialsPerCta partials (rows of a batch-1
     // launch have hundreds); maxc * wph bounds the partials of every row
-    const int64_t np_max = pl.maxc * pl.wph;
+    const int64_t np_max = pl.maxc * a.pw;
     int S = (int)((np_max + kMergePartialsPerCta - 1) / kMergePartialsPerCta);
     S = S < 1 ? 1 : S > kMergeMaxCluster ? kMergeMaxCluster : S;
     MergeArgs m{f.partials, f.out, f.o_stride_b, f.o_stride_h, f.Hq, pl.wph, pl.seq_pos, pl.W,
-                pl.maxc, S};
+                pl.maxc, a.pw, S};
     cudaLaunchAttribute mattr[2];
     mattr[0] = attr[0];
     mattr[1].id = cudaLaunchAttributeClusterDimension;
