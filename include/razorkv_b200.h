@@ -30,6 +30,8 @@
  *   rkv_release_pages         the storage release implied by razorkv/cache.py:356-358
  *   rkv_gather_tokens         materialises the contiguous key_cache/value_cache tensors of
  *                             razorkv/cache.py:89-91 from the paged layout
+ *   rkv_reindex_batch         razorkv/cache.py:198-229 (batch_repeat_interleave,
+ *                             batch_select_indices, reorder_cache) on the live pages only
  *   rkv_append_score_pool     razorkv/cache.py:361-393 and :322-331 (append, score, page
  *                             max-pool of a compacting decode step, one pass over K)
  *   rkv_select_compact_pages  razorkv/cache.py:333-359 (selection and pointer-only
@@ -400,6 +402,25 @@ int rkv_salience_apply_peer(const rkv_kv_layout* kv, const rkv_salience* sal,
  * receives the salience. */
 int rkv_gather_tokens(const rkv_kv_layout* kv, int which, void* dst, const rkv_salience* sal,
                       float* sal_dst, void* stream);
+
+/* Batch reindex of a cache pool's live pages: the index_select along the batch dimension
+ * behind razorkv/cache.py:198-206 (batch_repeat_interleave), :208-218 (batch_select_indices)
+ * and :220-229 (reorder_cache).  For every slot in slots[0 .. num_listed), row b of dst
+ * becomes row index[b] of src, for K, V (when both layouts have one) and the salience (when
+ * both salience pointers are given).  src and dst are pools [slots, B, Hkv, P, D]: each
+ * (slot, sequence) plane must be contiguous (stride_t == D, stride_h == P*D); their
+ * page_table and num_tokens are not used.  index holds dst->batch device entries in
+ * [0, src->batch).  dst may be src itself (same batch and strides): the rows are then
+ * permuted in place, and a row whose index is its own is neither read nor written.  List
+ * each slot at most once, and only slots whose contents matter (the pages of the layers'
+ * page tables): unlisted slots of dst are left as they are.  err (optional device int32,
+ * e.g. a workspace's error flag) is set to 2 when a listed slot is outside the pools or an
+ * index is outside [0, src->batch); such a slot or row is left unchanged.  Batches above
+ * about 3000 rows return RKV_ERR_UNSUPPORTED. */
+int rkv_reindex_batch(const rkv_kv_layout* src, const rkv_salience* src_sal,
+                      const rkv_kv_layout* dst, const rkv_salience* dst_sal,
+                      const int64_t* index, const int64_t* slots, int64_t num_listed,
+                      int* err, void* stream);
 
 #ifdef __cplusplus
 }

@@ -105,6 +105,8 @@ _SIGNATURES = {
     "rkv_release_pages": (ctypes.c_int, [c_vp, c_i64, c_vp, c_i64, c_vp]),
     "rkv_gather_tokens": (ctypes.c_int, [P(KVLayout), ctypes.c_int, c_vp, P(Salience), c_vp,
                                          c_vp]),
+    "rkv_reindex_batch": (ctypes.c_int, [P(KVLayout), P(Salience), P(KVLayout), P(Salience),
+                                         c_vp, c_vp, c_i64, c_vp, c_vp]),
     "rkv_append_partial": (ctypes.c_int, [P(KVLayout), c_vp, c_vp, c_i64, c_i64, c_i64, c_i64,
                                           c_i64, c_vp, c_vp, c_i64, ctypes.c_int, P(Exchange),
                                           c_vp]),
@@ -161,7 +163,8 @@ class RazorKVError(RuntimeError):
 # Codes a decode kernel leaves in a workspace's error flag (read by Workspace.check_errors).
 DEVICE_ERRORS = {
     1: "a bounded wait inside a decode kernel gave up (the launch's output is incomplete)",
-    2: "a page-table entry lies outside the page pool (that page was read as slot 0)",
+    2: "a page-table entry lies outside the page pool (that page was read as slot 0), or a "
+       "batch reindex named a slot or a row outside the pool (that slot or row was left as it was)",
 }
 
 

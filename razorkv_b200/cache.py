@@ -1025,14 +1025,49 @@ class PagedRazorKVCache(BaseCacheClass):
             self._free = torch.arange(self._slots - 1, -1, -1, dtype=torch.int64, device=self._device)
             self._free_top = self._slots
 
+    def _live_slots(self) -> torch.Tensor:
+        """Physical slots that hold retained pages (each once: no slot serves two layers)."""
+        live = [self._pt[l][: self._pages(n)] for l, n in enumerate(self._n) if n]
+        if not live:
+            return torch.empty(0, dtype=torch.int64, device=self._device)
+        return torch.cat(live)
+
     def _reindex_batch(self, index: torch.Tensor):
+        """Row b of every live page becomes row index[b] (``rkv_reindex_batch``).
+
+        The same batch size permutes the pool in place and touches only the rows whose index
+        differs from their own; a new batch size gathers the live pages into a new pool.
+        Free slots are never copied.  An index outside [0, B) raises ``DeviceError`` at the
+        next ``check_errors`` (the row keeps its old contents)."""
         self._flush_pending()
-        idx = index.to(self._device)
-        self._k = self._k.index_select(1, idx).contiguous()
-        self._v = self._v.index_select(1, idx).contiguous()
-        self._s = self._s.index_select(1, idx).contiguous()
-        self._B = self._k.shape[1]
-        self._pool_changed()
+        lib = _lib.load()
+        idx = index.to(device=self._device, dtype=torch.int64).reshape(-1).contiguous()
+        new_b = idx.numel()
+        slots = self._live_slots()
+        flag = Workspace._flag(Workspace.get(self._device, 1 << 20))
+        P = self.config.page_size
+        src = KVLayout(self._k.data_ptr(), self._v.data_ptr(), dtype_code(self._dtype), self._D,
+                       self._B, self._Hkv, self._k.stride(1), self._k.stride(2),
+                       self._k.stride(0), self._k.stride(3), P, self._slots, None, 0, 0)
+        src_sal = self._salience()
+        if new_b == self._B:
+            k, v, s = self._k, self._v, self._s
+        else:
+            shape = (self._slots, new_b, self._Hkv, P, self._D)
+            k = torch.zeros(shape, dtype=self._dtype, device=self._device)
+            v = torch.zeros(shape, dtype=self._dtype, device=self._device)
+            s = torch.zeros((self._slots, new_b, P), dtype=torch.float32, device=self._device)
+        dst = KVLayout(k.data_ptr(), v.data_ptr(), dtype_code(self._dtype), self._D, new_b,
+                       self._Hkv, k.stride(1), k.stride(2), k.stride(0), k.stride(3), P,
+                       self._slots, None, 0, 0)
+        dst_sal = Salience(s.data_ptr(), s.stride(1), s.stride(0))
+        st = lib.rkv_reindex_batch(src, src_sal, dst, dst_sal, idx.data_ptr(), slots.data_ptr(),
+                                   slots.numel(), flag.data_ptr(), self._stream())
+        check(st, "rkv_reindex_batch")
+        if new_b != self._B:
+            self._k, self._v, self._s = k, v, s
+            self._B = new_b
+            self._pool_changed()
 
     def batch_repeat_interleave(self, repeats: int) -> None:
         """razorkv/cache.py:198-206 (page tables are shared by every sequence)."""

@@ -756,4 +756,71 @@ int rkv_gather_tokens(const rkv_kv_layout* kv, int which, void* dst, const rkv_s
     return status_of(launch_gather(p, S(stream)));
 }
 
+int rkv_reindex_batch(const rkv_kv_layout* src, const rkv_salience* src_sal,
+                      const rkv_kv_layout* dst, const rkv_salience* dst_sal,
+                      const int64_t* index, const int64_t* slots, int64_t num_listed,
+                      int* err, void* stream) {
+    int st = check_kv(src, false);
+    if (st || (st = check_kv(dst, false))) return st;
+    if (num_listed < 0 || (num_listed > 0 && !slots) || (dst->batch > 0 && !index))
+        return RKV_ERR_INVALID_ARGUMENT;
+    if (src->dtype != dst->dtype || src->head_dim != dst->head_dim ||
+        src->num_kv_heads != dst->num_kv_heads || src->page_size != dst->page_size ||
+        src->page_size < 1 || src->num_slots < 0 || dst->num_slots < 0)
+        return RKV_ERR_INVALID_ARGUMENT;
+    if (!src->v != !dst->v || !src_sal != !dst_sal || (src_sal && (!src_sal->s || !dst_sal->s)))
+        return RKV_ERR_INVALID_ARGUMENT;
+    const int64_t D = src->head_dim, P = src->page_size;
+    // every (slot, sequence) plane of K and V must be one contiguous run of Hkv*P*D elements
+    for (const rkv_kv_layout* l : {src, dst})
+        if (l->stride_t != D || l->stride_h != P * D) return RKV_ERR_UNSUPPORTED;
+    const bool in_place = src->k == dst->k;
+    if (in_place != (src->v == dst->v) ||
+        (src_sal && in_place != (src_sal->s == dst_sal->s)))
+        return RKV_ERR_INVALID_ARGUMENT;
+    if (in_place && (src->batch != dst->batch || src->stride_b != dst->stride_b ||
+                     src->stride_p != dst->stride_p ||
+                     (src_sal && (src_sal->stride_b != dst_sal->stride_b ||
+                                  src_sal->stride_p != dst_sal->stride_p))))
+        return RKV_ERR_INVALID_ARGUMENT;
+    const int64_t eb = elt_bytes(src->dtype);
+    ReindexParams p{};
+    p.src[0] = static_cast<const char*>(src->k); p.dst[0] = static_cast<char*>(const_cast<void*>(dst->k));
+    p.src[1] = static_cast<const char*>(src->v); p.dst[1] = static_cast<char*>(const_cast<void*>(dst->v));
+    p.src[2] = src_sal ? reinterpret_cast<const char*>(src_sal->s) : nullptr;
+    p.dst[2] = dst_sal ? reinterpret_cast<char*>(dst_sal->s) : nullptr;
+    const int64_t kv_row = src->num_kv_heads * P * D * eb;
+    for (int w = 0; w < 2; ++w) {
+        p.row_bytes[w] = p.src[w] ? kv_row : 0;
+        p.src_slot_stride[w] = src->stride_p * eb; p.src_b_stride[w] = src->stride_b * eb;
+        p.dst_slot_stride[w] = dst->stride_p * eb; p.dst_b_stride[w] = dst->stride_b * eb;
+    }
+    p.row_bytes[2] = src_sal ? P * 4 : 0;
+    if (src_sal) {
+        p.src_slot_stride[2] = src_sal->stride_p * 4; p.src_b_stride[2] = src_sal->stride_b * 4;
+        p.dst_slot_stride[2] = dst_sal->stride_p * 4; p.dst_b_stride[2] = dst_sal->stride_b * 4;
+    }
+    // widest access every base, stride and row length allows
+    int vec = 16;
+    for (int w = 0; w < 3; ++w) {
+        if (!p.src[w]) continue;
+        const int64_t vals[] = {(int64_t)(uintptr_t)p.src[w], (int64_t)(uintptr_t)p.dst[w],
+                                p.src_slot_stride[w], p.src_b_stride[w], p.dst_slot_stride[w],
+                                p.dst_b_stride[w], p.row_bytes[w]};
+        for (int64_t x : vals) {
+            while (vec > 2 && x % vec != 0) vec = vec == 16 ? 4 : 2;
+        }
+    }
+    p.vec = vec;
+    p.chunk = reindex_chunk_bytes(dst->batch, kv_row > P * 4 ? kv_row : P * 4, vec);
+    if (dst->batch > 0 && p.chunk == 0) return RKV_ERR_UNSUPPORTED;
+    for (int w = 0; w < 3; ++w)
+        p.chunks[w] = p.chunk ? (p.row_bytes[w] + p.chunk - 1) / p.chunk : 0;
+    p.src_B = src->batch; p.dst_B = dst->batch;
+    p.num_slots = src->num_slots < dst->num_slots ? src->num_slots : dst->num_slots;
+    p.index = index; p.slots = slots; p.n_listed = num_listed; p.err = err;
+    p.in_place = in_place ? 1 : 0;
+    return status_of(launch_reindex(p, S(stream)));
+}
+
 }  // extern "C"

@@ -626,6 +626,126 @@ __global__ void gather_kernel(GatherParams p) {
 }
 
 // ------------------------------------------------------------------------------------------
+// Batch reindex of the pool's live slots (razorkv/cache.py:198-229: batch_repeat_interleave,
+// batch_select_indices and reorder_cache index_select the batch dimension of every layer's
+// K, V and salience).  Only the slots the page tables reference are listed, so the bytes
+// moved are those of the retained pages, not of the whole pool.  A work item is (listed slot,
+// chunk of one pool's row); each CTA walks items with a grid stride.  For an item it reads
+// the chunk of source row index[b] of every moving destination row b into shared memory and
+// then writes the staged chunks, so with src == dst the rows are permuted in place.  In
+// place, a row whose index is its own does not move: a beam that keeps its own history costs
+// nothing, and a call whose rows all stay returns at once.
+// ------------------------------------------------------------------------------------------
+constexpr int kReindexThreads = 256;
+constexpr int kReindexSmem = 48 * 1024;   // per CTA: moving-row lists + staged chunks
+
+__host__ __device__ inline int64_t reindex_list_bytes(int64_t dst_B) {
+    return ((dst_B * 8 + 15) / 16) * 16;
+}
+
+// Threads split into rows_per_pass groups of lanes_per_row lanes; lane e of a group handles
+// vectors e, e + lanes_per_row, ... of its rows, so no element index needs a division.
+template <typename T>
+__device__ __forceinline__ void reindex_rows(const ReindexParams& p, int which, int64_t slot,
+                                             int64_t off, int len, const int* act_dst,
+                                             const int* act_src, int n_act, T* stage) {
+    const int nv = len / (int)sizeof(T);
+    const int cv = (int)(p.chunk / (int64_t)sizeof(T));
+    const int lpr = nv < kReindexThreads ? nv : kReindexThreads;
+    const int rpp = kReindexThreads / lpr;
+    const int my_r = threadIdx.x / lpr;
+    const int my_e = threadIdx.x - my_r * lpr;
+    const bool on = my_r < rpp;
+    const char* sbase = p.src[which] + slot * p.src_slot_stride[which] + off;
+    constexpr int U = 8;
+    if (on) {
+        for (int j0 = my_r; j0 < n_act; j0 += U * rpp) {
+            for (int e = my_e; e < nv; e += lpr) {
+                T r[U];
+                #pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int j = j0 + u * rpp;
+                    if (j < n_act)
+                        r[u] = reinterpret_cast<const T*>(sbase + act_src[j] * p.src_b_stride[which])[e];
+                }
+                #pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int j = j0 + u * rpp;
+                    if (j < n_act) stage[j * cv + e] = r[u];
+                }
+            }
+        }
+    }
+    __syncthreads();
+    char* dbase = p.dst[which] + slot * p.dst_slot_stride[which] + off;
+    if (on) {
+        for (int j = my_r; j < n_act; j += rpp) {
+            T* drow = reinterpret_cast<T*>(dbase + act_dst[j] * p.dst_b_stride[which]);
+            for (int e = my_e; e < nv; e += lpr) drow[e] = stage[j * cv + e];
+        }
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kReindexThreads, 4) reindex_kernel(ReindexParams p) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ int warp_count[kReindexThreads / 32];
+    int* act_dst = reinterpret_cast<int*>(smem);
+    int* act_src = act_dst + p.dst_B;
+    unsigned char* stage = smem + reindex_list_bytes(p.dst_B);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const bool report = blockIdx.x == 0 && p.err;
+    // moving rows, ascending b: (destination row, source row)
+    int n_act = 0;
+    for (int b0 = 0; b0 < p.dst_B; b0 += kReindexThreads) {
+        const int b = b0 + threadIdx.x;
+        int src = -1;
+        if (b < p.dst_B) {
+            const int64_t s = p.index[b];
+            if (s < 0 || s >= p.src_B) {
+                if (report) atomicExch(p.err, 2);
+            } else if (!(p.in_place && s == b)) {
+                src = (int)s;
+            }
+        }
+        const unsigned ballot = __ballot_sync(0xffffffffu, src >= 0);
+        if (lane == 0) warp_count[warp] = __popc(ballot);
+        __syncthreads();
+        int before = 0, all = 0;
+        for (int w = 0; w < kReindexThreads / 32; ++w) {
+            before += w < warp ? warp_count[w] : 0;
+            all += warp_count[w];
+        }
+        if (src >= 0) {
+            const int pos = n_act + before + __popc(ballot & ((1u << lane) - 1u));
+            act_dst[pos] = b;
+            act_src[pos] = src;
+        }
+        n_act += all;
+        __syncthreads();
+    }
+    if (n_act == 0) return;
+    const int64_t ych = p.chunks[0] + p.chunks[1] + p.chunks[2];
+    const int64_t items = p.n_listed * ych;
+    for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
+        const int64_t li = it / ych;
+        int64_t c = it - li * ych;
+        const int64_t slot = p.slots[li];
+        if (slot < 0 || slot >= p.num_slots) {
+            if (threadIdx.x == 0 && c == 0 && p.err) atomicExch(p.err, 2);
+            continue;
+        }
+        int which = 0;
+        while (which < 2 && c >= p.chunks[which]) { c -= p.chunks[which]; ++which; }
+        const int64_t off = c * p.chunk;
+        const int len = (int)min(p.chunk, p.row_bytes[which] - off);
+        reindex_rows<T>(p, which, slot, off, len, act_dst, act_src, n_act,
+                        reinterpret_cast<T*>(stage));
+        __syncthreads();   // the next item restages
+    }
+}
+
+// ------------------------------------------------------------------------------------------
 // Salience update of a head-sharded step (razorkv/cache.py:239-247 and :282-287 once the
 // ranks' partial results are combined): the exchange block holds, after the MAX over the
 // ranks of the head group, every token's resonance key (max over all query heads) and the
@@ -851,6 +971,36 @@ cudaError_t launch_gather(const GatherParams& p, cudaStream_t st) {
     int64_t total = p.B * p.Hkv * p.N * p.D;
     if (total == 0) return cudaSuccess;
     gather_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(p);
+    return counted(cudaGetLastError(), 1);
+}
+
+int64_t reindex_chunk_bytes(int64_t dst_B, int64_t max_row_bytes, int vec) {
+    if (dst_B < 1) return 0;
+    const int64_t avail = (kReindexSmem - reindex_list_bytes(dst_B)) / dst_B;
+    if (avail < vec) return 0;
+    int64_t chunk = vec;
+    while (chunk * 2 <= avail) chunk *= 2;
+    const int64_t row = (max_row_bytes + vec - 1) / vec * vec;
+    return chunk < row ? chunk : row;
+}
+
+cudaError_t launch_reindex(const ReindexParams& p, cudaStream_t st) {
+    const int64_t items = p.n_listed * (p.chunks[0] + p.chunks[1] + p.chunks[2]);
+    if (items == 0 || p.dst_B == 0) return cudaSuccess;
+    const size_t smem = (size_t)(reindex_list_bytes(p.dst_B) + p.dst_B * p.chunk);
+    void (*kern)(ReindexParams) = p.vec == 16 ? reindex_kernel<uint4>
+                                  : p.vec == 4 ? reindex_kernel<uint32_t>
+                                               : reindex_kernel<uint16_t>;
+    // one resident wave: every CTA walks its items until the list ends
+    int dev = 0, sms = 148, per_sm = 1;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kReindexThreads, smem) !=
+            cudaSuccess || per_sm < 1)
+        per_sm = 1;
+    int64_t ctas = (int64_t)sms * per_sm;
+    if (ctas > items) ctas = items;
+    kern<<<(unsigned)ctas, kReindexThreads, smem, st>>>(p);
     return counted(cudaGetLastError(), 1);
 }
 

@@ -114,6 +114,23 @@ struct GatherParams {
     const float* sal; int64_t sal_stride_b, sal_stride_p; float* sal_dst;
 };
 
+// Batch reindex of listed pool slots (K, V, salience): row b of dst <- row index[b] of src.
+// A "row" is the bytes of one (slot, sequence) plane of a pool; strides are in bytes.
+struct ReindexParams {
+    const char* src[3]; char* dst[3];
+    int64_t src_slot_stride[3], src_b_stride[3];
+    int64_t dst_slot_stride[3], dst_b_stride[3];
+    int64_t row_bytes[3];
+    int64_t chunks[3];          // chunks of `chunk` bytes per row of each pool
+    int64_t chunk;
+    int64_t src_B, dst_B, num_slots;
+    const int64_t* index;       // [dst_B]
+    const int64_t* slots; int64_t n_listed;
+    int* err;                   // optional: 2 on a slot or index out of range
+    int in_place;               // src == dst: rows whose index is their own are skipped
+    int vec;                    // bytes per access: 16, 4 or 2
+};
+
 // Fused score + attention for the sm_100a fast path (rkv_decode_sm100.cu).
 struct FusedParams {
     const void* q; int64_t q_stride_b, q_stride_h;
@@ -163,6 +180,9 @@ cudaError_t launch_compact_tokens(const CompactTokensParams& p, cudaStream_t st)
 cudaError_t launch_release(const int64_t* pages, int64_t n, int64_t* free_stack, int64_t top,
                            cudaStream_t st);
 cudaError_t launch_gather(const GatherParams& p, cudaStream_t st);
+// chunk size for a reindex into dst_B rows (0: dst_B too large for the staging buffer)
+int64_t reindex_chunk_bytes(int64_t dst_B, int64_t max_row_bytes, int vec);
+cudaError_t launch_reindex(const ReindexParams& p, cudaStream_t st);
 cudaError_t launch_apply(const ApplyParams& p, cudaStream_t st);
 cudaError_t launch_apply_peer(const PeerApplyParams& p, cudaStream_t st);
 
