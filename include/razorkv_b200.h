@@ -76,7 +76,13 @@ typedef enum rkv_salience_init { RKV_SAL_NORM = 0, RKV_SAL_UNIFORM = 1 } rkv_sal
  * or, with page_table == NULL, at base + b*stride_b + h*stride_h + t*stride_t.
  * Strides are in elements.  For the reference's paged operator the storage is
  * [B, Hkv, MAXP, P, D]; for the cache pool it is [slots, B, Hkv, P, D] with one page table
- * shared by all sequences (pt_stride_b = 0). */
+ * shared by all sequences (pt_stride_b = 0).
+ * row_map (optional; pool storage with a shared page table, not read without a page table):
+ * int32 [num_slots][batch].  Sequence b's rows of the page in slot s are stored in the pool's
+ * sequence row row_map[s*batch + b] instead of row b, so sequences can share a page (beam
+ * search: rkv_reindex_batch rewrites the map instead of moving K/V).  Rows are only written
+ * through identity entries: an appended token's page must map b -> b, and a slot taken from
+ * the free stack has its entries reset to identity by the call that takes it. */
 typedef struct rkv_kv_layout {
     const void* k;
     const void* v;               /* may be NULL for score-only calls */
@@ -90,6 +96,7 @@ typedef struct rkv_kv_layout {
     const int64_t* page_table;   /* NULL = contiguous tokens */
     int64_t pt_stride_b;         /* 0 = table shared by every sequence */
     int64_t num_tokens;          /* valid tokens per sequence */
+    int32_t* row_map;            /* NULL = sequence b in row b (see above) */
 } rkv_kv_layout;
 
 /* Query rows [B, Hq, QL, D]: element (b, h, t, d) at q + b*stride_b + h*stride_h + t*stride_t + d. */
@@ -405,22 +412,29 @@ int rkv_gather_tokens(const rkv_kv_layout* kv, int which, void* dst, const rkv_s
 
 /* Batch reindex of a cache pool's live pages: the index_select along the batch dimension
  * behind razorkv/cache.py:198-206 (batch_repeat_interleave), :208-218 (batch_select_indices)
- * and :220-229 (reorder_cache).  For every slot in slots[0 .. num_listed), row b of dst
- * becomes row index[b] of src, for K, V (when both layouts have one) and the salience (when
+ * and :220-229 (reorder_cache).  Sequence b of dst becomes sequence index[b] of src on every
+ * slot in slots[0 .. num_listed), for K, V (when both layouts have one) and the salience (when
  * both salience pointers are given).  src and dst are pools [slots, B, Hkv, P, D]: each
  * (slot, sequence) plane must be contiguous (stride_t == D, stride_h == P*D); their
  * page_table and num_tokens are not used.  index holds dst->batch device entries in
- * [0, src->batch).  dst may be src itself (same batch and strides): the rows are then
- * permuted in place, and a row whose index is its own is neither read nor written.  List
- * each slot at most once, and only slots whose contents matter (the pages of the layers'
- * page tables): unlisted slots of dst are left as they are.  err (optional device int32,
- * e.g. a workspace's error flag) is set to 2 when a listed slot is outside the pools or an
- * index is outside [0, src->batch); such a slot or row is left unchanged.  Batches above
- * about 3000 rows return RKV_ERR_UNSUPPORTED. */
+ * [0, src->batch).
+ * Out of place (dst is another pool, any batch): every listed slot's rows are gathered
+ * through src->row_map (when set) and dst holds sequence b in row b (dst->row_map NULL).
+ * In place (dst == src, same batch and strides): the salience rows are permuted.  Without a
+ * row map the K/V rows are too.  With src->row_map set, only the first num_moved listed
+ * slots move their K/V rows (to identity rows: use it for every page that will still be
+ * written, i.e. each layer's last page); the other slots keep their K/V and their row map
+ * entries are rewritten, row_map[s][b] <- row_map[s][index[b]]: a page-table update, not a
+ * copy.  A row that would copy onto itself is neither read nor written.  List each slot at
+ * most once, and only slots whose contents matter (the pages of the layers' page tables):
+ * unlisted slots are left as they are.  err (optional device int32, e.g. a workspace's error
+ * flag) is set to 2 when a listed slot is outside the pools or an index is outside
+ * [0, src->batch); such a slot or row is left unchanged.  Batches above about 1500 rows
+ * return RKV_ERR_UNSUPPORTED. */
 int rkv_reindex_batch(const rkv_kv_layout* src, const rkv_salience* src_sal,
                       const rkv_kv_layout* dst, const rkv_salience* dst_sal,
                       const int64_t* index, const int64_t* slots, int64_t num_listed,
-                      int* err, void* stream);
+                      int64_t num_moved, int* err, void* stream);
 
 #ifdef __cplusplus
 }

@@ -35,7 +35,7 @@ class KVLayout(ctypes.Structure):
         ("batch", c_i64), ("num_kv_heads", c_i64),
         ("stride_b", c_i64), ("stride_h", c_i64), ("stride_p", c_i64), ("stride_t", c_i64),
         ("page_size", c_i64), ("num_slots", c_i64), ("page_table", c_vp),
-        ("pt_stride_b", c_i64), ("num_tokens", c_i64),
+        ("pt_stride_b", c_i64), ("num_tokens", c_i64), ("row_map", c_vp),
     ]
 
 
@@ -106,7 +106,7 @@ _SIGNATURES = {
     "rkv_gather_tokens": (ctypes.c_int, [P(KVLayout), ctypes.c_int, c_vp, P(Salience), c_vp,
                                          c_vp]),
     "rkv_reindex_batch": (ctypes.c_int, [P(KVLayout), P(Salience), P(KVLayout), P(Salience),
-                                         c_vp, c_vp, c_i64, c_vp, c_vp]),
+                                         c_vp, c_vp, c_i64, c_i64, c_vp, c_vp]),
     "rkv_append_partial": (ctypes.c_int, [P(KVLayout), c_vp, c_vp, c_i64, c_i64, c_i64, c_i64,
                                           c_i64, c_vp, c_vp, c_i64, ctypes.c_int, P(Exchange),
                                           c_vp]),

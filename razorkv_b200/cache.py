@@ -172,6 +172,9 @@ class PagedRazorKVCache(BaseCacheClass):
         self._free = None
         self._free_top = 0
         self._slots = 0
+        # row map [slots, B] int32 (None = sequence b in row b): created by the first in-place
+        # reorder_cache, which then shares pages between beams instead of copying them
+        self._rowmap: Optional[torch.Tensor] = None
         self._B = self._Hkv = self._D = 0
         self._dtype = None
         self._device = None
@@ -338,6 +341,10 @@ class PagedRazorKVCache(BaseCacheClass):
             free[new - old: new - old + self._free_top].copy_(free[: self._free_top].clone())
         free[: new - old].copy_(added)
         self._k, self._v, self._s, self._free = k, v, s, free
+        if self._rowmap is not None:
+            rm = torch.arange(self._B, dtype=torch.int32, device=dev).repeat(new, 1)
+            rm[:old].copy_(self._rowmap)
+            self._rowmap = rm
         self._free_top += new - old
         self._slots = new
         self._pool_changed()
@@ -372,7 +379,8 @@ class PagedRazorKVCache(BaseCacheClass):
         n = self._n[layer_idx] if n_tokens is None else n_tokens
         return KVLayout(k.data_ptr(), self._v.data_ptr(), dtype_code(self._dtype), self._D,
                         self._B, self._Hkv, k.stride(1), k.stride(2), k.stride(0), k.stride(3),
-                        self.config.page_size, self._slots, self._pt[layer_idx].data_ptr(), 0, n)
+                        self.config.page_size, self._slots, self._pt[layer_idx].data_ptr(), 0, n,
+                        self._rowmap.data_ptr() if self._rowmap is not None else None)
 
     def _salience(self) -> Salience:
         return Salience(self._s.data_ptr(), self._s.stride(1), self._s.stride(0))
@@ -1001,6 +1009,10 @@ class PagedRazorKVCache(BaseCacheClass):
             check(st, "rkv_release_pages")
             self._free_top += old_pages - new_pages
         self._n[layer_idx] = new_n
+        if self._rowmap is not None and new_pages > 0:
+            # the new last page will be written again: give every sequence its own rows
+            last = self._pt[layer_idx][new_pages - 1: new_pages]
+            self._reindex_rows(torch.arange(self._B, device=self._device), last, 1)
 
     def crop(self, tokens_to_remove: int = 0) -> None:
         """razorkv/cache.py:177-188: drop the most recent tokens of every layer."""
@@ -1021,53 +1033,80 @@ class PagedRazorKVCache(BaseCacheClass):
         self._layers.clear()
         self._seen_tokens = 0
         self._lay_cache.clear()
+        self._rowmap = None
         if self._k is not None:
             self._free = torch.arange(self._slots - 1, -1, -1, dtype=torch.int64, device=self._device)
             self._free_top = self._slots
 
-    def _live_slots(self) -> torch.Tensor:
-        """Physical slots that hold retained pages (each once: no slot serves two layers)."""
-        live = [self._pt[l][: self._pages(n)] for l, n in enumerate(self._n) if n]
-        if not live:
-            return torch.empty(0, dtype=torch.int64, device=self._device)
-        return torch.cat(live)
+    def _live_slots(self) -> Tuple[torch.Tensor, int]:
+        """Physical slots that hold retained pages, each layer's last page first, and the number
+        of those last pages.  Each slot appears once: no slot serves two layers."""
+        last, rest = [], []
+        for l, n in enumerate(self._n):
+            if n:
+                pages = self._pages(n)
+                last.append(self._pt[l][pages - 1: pages])
+                rest.append(self._pt[l][: pages - 1])
+        if not last:
+            return torch.empty(0, dtype=torch.int64, device=self._device), 0
+        return torch.cat(last + rest), len(last)
+
+    def _pool_layout(self, k, v, batch, rowmap) -> KVLayout:
+        return KVLayout(k.data_ptr(), v.data_ptr(), dtype_code(self._dtype), self._D, batch,
+                        self._Hkv, k.stride(1), k.stride(2), k.stride(0), k.stride(3),
+                        self.config.page_size, self._slots, None, 0, 0,
+                        rowmap.data_ptr() if rowmap is not None else None)
+
+    def _reindex_rows(self, idx: torch.Tensor, slots: torch.Tensor, num_moved: int):
+        """In-place ``rkv_reindex_batch`` over ``slots`` (the first ``num_moved`` move their
+        K/V rows; the others only have their row map rewritten)."""
+        lib = _lib.load()
+        idx = idx.to(device=self._device, dtype=torch.int64).reshape(-1).contiguous()
+        flag = Workspace._flag(Workspace.get(self._device, 1 << 20))
+        lay = self._pool_layout(self._k, self._v, self._B, self._rowmap)
+        sal = self._salience()
+        st = lib.rkv_reindex_batch(lay, sal, lay, sal, idx.data_ptr(), slots.data_ptr(),
+                                   slots.numel(), num_moved, flag.data_ptr(), self._stream())
+        check(st, "rkv_reindex_batch")
 
     def _reindex_batch(self, index: torch.Tensor):
-        """Row b of every live page becomes row index[b] (``rkv_reindex_batch``).
+        """Sequence b becomes sequence index[b] (``rkv_reindex_batch`` over the live pages).
 
-        The same batch size permutes the pool in place and touches only the rows whose index
-        differs from their own; a new batch size gathers the live pages into a new pool.
-        Free slots are never copied.  An index outside [0, B) raises ``DeviceError`` at the
-        next ``check_errors`` (the row keeps its old contents)."""
+        The same batch size (beam search) is a page-table update: every full page keeps its
+        K/V and the row map points each sequence at the row of the beam it continues; only
+        the salience rows (every beam's EWMA diverges) and each layer's last page (it will be
+        written again) move.  A new batch size gathers the live pages into a new pool.  Free
+        slots are never copied.  An index outside [0, B) raises ``DeviceError`` at the next
+        ``check_errors`` (that sequence keeps its old contents)."""
         self._flush_pending()
-        lib = _lib.load()
         idx = index.to(device=self._device, dtype=torch.int64).reshape(-1).contiguous()
         new_b = idx.numel()
-        slots = self._live_slots()
+        slots, n_last = self._live_slots()
+        if new_b == self._B:
+            if self._rowmap is None:
+                self._rowmap = torch.arange(self._B, dtype=torch.int32,
+                                            device=self._device).repeat(self._slots, 1)
+                self._pool_changed()
+            self._reindex_rows(idx, slots, n_last)
+            return
+        lib = _lib.load()
         flag = Workspace._flag(Workspace.get(self._device, 1 << 20))
         P = self.config.page_size
-        src = KVLayout(self._k.data_ptr(), self._v.data_ptr(), dtype_code(self._dtype), self._D,
-                       self._B, self._Hkv, self._k.stride(1), self._k.stride(2),
-                       self._k.stride(0), self._k.stride(3), P, self._slots, None, 0, 0)
-        src_sal = self._salience()
-        if new_b == self._B:
-            k, v, s = self._k, self._v, self._s
-        else:
-            shape = (self._slots, new_b, self._Hkv, P, self._D)
-            k = torch.zeros(shape, dtype=self._dtype, device=self._device)
-            v = torch.zeros(shape, dtype=self._dtype, device=self._device)
-            s = torch.zeros((self._slots, new_b, P), dtype=torch.float32, device=self._device)
-        dst = KVLayout(k.data_ptr(), v.data_ptr(), dtype_code(self._dtype), self._D, new_b,
-                       self._Hkv, k.stride(1), k.stride(2), k.stride(0), k.stride(3), P,
-                       self._slots, None, 0, 0)
+        shape = (self._slots, new_b, self._Hkv, P, self._D)
+        k = torch.zeros(shape, dtype=self._dtype, device=self._device)
+        v = torch.zeros(shape, dtype=self._dtype, device=self._device)
+        s = torch.zeros((self._slots, new_b, P), dtype=torch.float32, device=self._device)
+        src = self._pool_layout(self._k, self._v, self._B, self._rowmap)
+        dst = self._pool_layout(k, v, new_b, None)
         dst_sal = Salience(s.data_ptr(), s.stride(1), s.stride(0))
-        st = lib.rkv_reindex_batch(src, src_sal, dst, dst_sal, idx.data_ptr(), slots.data_ptr(),
-                                   slots.numel(), flag.data_ptr(), self._stream())
+        st = lib.rkv_reindex_batch(src, self._salience(), dst, dst_sal, idx.data_ptr(),
+                                   slots.data_ptr(), slots.numel(), slots.numel(),
+                                   flag.data_ptr(), self._stream())
         check(st, "rkv_reindex_batch")
-        if new_b != self._B:
-            self._k, self._v, self._s = k, v, s
-            self._B = new_b
-            self._pool_changed()
+        self._k, self._v, self._s = k, v, s
+        self._rowmap = None
+        self._B = new_b
+        self._pool_changed()
 
     def batch_repeat_interleave(self, repeats: int) -> None:
         """razorkv/cache.py:198-206 (page tables are shared by every sequence)."""

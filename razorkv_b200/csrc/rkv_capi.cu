@@ -43,6 +43,9 @@ int check_kv(const rkv_kv_layout* kv, bool need_v) {
     if (kv->head_dim < 1 || kv->head_dim > kMaxHeadDim) return RKV_ERR_UNSUPPORTED;
     if (kv->batch < 0 || kv->num_kv_heads < 1 || kv->num_tokens < 0) return RKV_ERR_INVALID_ARGUMENT;
     if (kv->page_table && kv->page_size < 1) return RKV_ERR_INVALID_ARGUMENT;
+    // a row map describes a cache pool: one page table shared by every sequence (without a
+    // page table it is not read)
+    if (kv->row_map && kv->page_table && kv->pt_stride_b != 0) return RKV_ERR_INVALID_ARGUMENT;
     return RKV_OK;
 }
 
@@ -68,6 +71,7 @@ AttnParams attn_params(const rkv_query* q, const rkv_kv_layout* kv, float scale,
     p.stride_t = kv->stride_t; p.page_size = kv->page_size;
     p.page_table = kv->page_table; p.pt_stride_b = kv->pt_stride_b;
     p.num_slots = kv->page_table ? kv->num_slots : 0;
+    p.row_map = kv->row_map;
     p.scale = scale > 0.0f ? scale : (float)(1.0 / sqrt((double)kv->head_dim));
     p.causal = causal;
     p.out = out->out; p.out_dtype = out->dtype;
@@ -103,6 +107,7 @@ FusedParams fused_params(const rkv_query* q, const rkv_kv_layout* kv, const rkv_
     p.stride_b = kv->stride_b; p.stride_h = kv->stride_h; p.stride_p = kv->stride_p;
     p.stride_t = kv->stride_t; p.num_slots = kv->num_slots;
     p.page_table = kv->page_table; p.pt_stride_b = kv->pt_stride_b;
+    p.row_map = kv->row_map;
     p.sal = sal ? sal->s : nullptr;
     p.sal_stride_b = sal ? sal->stride_b : 0; p.sal_stride_p = sal ? sal->stride_p : 0;
     p.scale_r = resonance_scale(kv->head_dim);
@@ -224,6 +229,7 @@ static int append_impl(const rkv_kv_layout* kv, const rkv_salience* sal, const v
     p.page_table = page_table; p.free_stack = free_stack; p.free_top = free_top;
     p.salience_init = salience_init;
     p.xc = xc;
+    p.row_map = kv->row_map;
     {
         const int64_t eb = kv->dtype == RKV_F32 ? 4 : 2;
         const int64_t strides[7] = {new_stride_b, new_stride_h, new_stride_t, kv->stride_b,
@@ -274,6 +280,7 @@ static int score_impl(const rkv_query* q, const rkv_kv_layout* kv, const rkv_sal
     p.scale_r = resonance_scale(kv->head_dim);
     p.decay = decay; p.one_minus_decay = one_minus_decay; p.ewma = ewma;
     p.xc = xc;
+    p.row_map = kv->row_map;
     return status_of(launch_score(p, S(stream)));
 }
 
@@ -731,6 +738,7 @@ int rkv_compact_tokens(const rkv_kv_layout* kv, const rkv_salience* sal,
     p.old_pt = kv->page_table; p.new_pt = new_page_table; p.free_stack = free_stack;
     p.free_top = free_top; p.new_len = new_len; p.sink = sink; p.n_kept = k; p.kept = kept;
     p.sel_page_size = sel_page_size; p.hay_start = hay_start; p.tail_src_start = tail_src_start;
+    p.row_map = kv->row_map;
     return status_of(launch_compact_tokens(p, S(stream)));
 }
 
@@ -753,13 +761,14 @@ int rkv_gather_tokens(const rkv_kv_layout* kv, int which, void* dst, const rkv_s
     p.page_table = kv->page_table; p.pt_stride_b = kv->pt_stride_b;
     p.sal = sal ? sal->s : nullptr; p.sal_stride_b = sal ? sal->stride_b : 0;
     p.sal_stride_p = sal ? sal->stride_p : 0; p.sal_dst = sal_dst;
+    p.row_map = kv->row_map;
     return status_of(launch_gather(p, S(stream)));
 }
 
 int rkv_reindex_batch(const rkv_kv_layout* src, const rkv_salience* src_sal,
                       const rkv_kv_layout* dst, const rkv_salience* dst_sal,
                       const int64_t* index, const int64_t* slots, int64_t num_listed,
-                      int* err, void* stream) {
+                      int64_t num_moved, int* err, void* stream) {
     int st = check_kv(src, false);
     if (st || (st = check_kv(dst, false))) return st;
     if (num_listed < 0 || (num_listed > 0 && !slots) || (dst->batch > 0 && !index))
@@ -783,6 +792,11 @@ int rkv_reindex_batch(const rkv_kv_layout* src, const rkv_salience* src_sal,
                      (src_sal && (src_sal->stride_b != dst_sal->stride_b ||
                                   src_sal->stride_p != dst_sal->stride_p))))
         return RKV_ERR_INVALID_ARGUMENT;
+    // in place the row map is src's own; out of place dst gets sequence b in row b
+    if ((in_place && dst->row_map != src->row_map) || (!in_place && dst->row_map))
+        return RKV_ERR_INVALID_ARGUMENT;
+    if (num_moved < 0 || num_moved > num_listed) return RKV_ERR_INVALID_ARGUMENT;
+    const bool compose = in_place && src->row_map != nullptr;
     const int64_t eb = elt_bytes(src->dtype);
     ReindexParams p{};
     p.src[0] = static_cast<const char*>(src->k); p.dst[0] = static_cast<char*>(const_cast<void*>(dst->k));
@@ -820,7 +834,12 @@ int rkv_reindex_batch(const rkv_kv_layout* src, const rkv_salience* src_sal,
     p.num_slots = src->num_slots < dst->num_slots ? src->num_slots : dst->num_slots;
     p.index = index; p.slots = slots; p.n_listed = num_listed; p.err = err;
     p.in_place = in_place ? 1 : 0;
-    return status_of(launch_reindex(p, S(stream)));
+    p.row_map = src->row_map;
+    p.n_moved = compose ? num_moved : num_listed;
+    const cudaError_t e = launch_reindex(p, S(stream));
+    if (e != cudaSuccess || !compose) return status_of(e);
+    return status_of(launch_row_map_compose(src->row_map, src->batch, index, slots, num_listed,
+                                            num_moved, p.num_slots, S(stream)));
 }
 
 }  // extern "C"

@@ -70,11 +70,21 @@ struct TokenMap {
     int64_t stride_p;            // elements between physical pages
     int64_t stride_t;            // elements between tokens inside a page
     int64_t num_slots = 0;       // physical pages in the storage (0: ids not checked)
+    // optional row map of a cache pool ([slots][batch] int32): sequence `seq` of the page in
+    // slot s lives in row row_map[s * batch + seq]; offset() then adds (row - seq) * stride_b
+    // to a base that already holds seq * stride_b.  Entries outside [0, batch) read row seq.
+    const int32_t* row_map = nullptr;
+    int64_t batch = 0, seq = 0, stride_b = 0;
     __device__ __forceinline__ int64_t offset(int64_t t) const {
         if (page_table == nullptr) return t * stride_t;
         int64_t pg = page_table[t / page_size];
         if (num_slots > 0 && (pg < 0 || pg >= num_slots)) pg = 0;
-        return pg * stride_p + (t % page_size) * stride_t;
+        int64_t off = pg * stride_p + (t % page_size) * stride_t;
+        if (row_map != nullptr) {
+            const int64_t r = row_map[pg * batch + seq];
+            if (r >= 0 && r < batch) off += (r - seq) * stride_b;
+        }
+        return off;
     }
 };
 

@@ -72,6 +72,9 @@ struct DevArgs {
     // the CTA first (one-sequence launches of the tensor-core-logit instances)
     int pw;
     const int64_t* pt; int64_t pt_stride_b; int64_t num_slots;
+    // pool row map [num_slots][B] (nullptr: sequence b in row b); the appended token's page
+    // maps every sequence to its own row
+    int32_t* row_map;
     float* sal; int64_t sal_stride_b, sal_stride_p;
     float scale_r, logit_log2, decay, omd;
     int attend, score, sal_bulk;
@@ -284,6 +287,14 @@ __device__ __forceinline__ void canon_dots4(uint32_t kb, int half_bytes, const i
     }
 #pragma unroll
     for (int r = 0; r < 4; ++r) v[r] = part[r];
+}
+
+// Row of sequence b in the page in slot v: the row map's entry, or b (no map, an id outside
+// the pool, or an entry outside [0, B)).
+__device__ __forceinline__ int map_row(const DevArgs& a, int64_t v, int64_t b) {
+    if (a.row_map == nullptr || v < 0 || v >= a.num_slots) return (int)b;
+    const int r = __ldg(a.row_map + v * a.B + b);
+    return (r >= 0 && r < a.B) ? r : (int)b;
 }
 
 // MODE 0: one query; its canonical-order scores give the resonance and the attention logits.
@@ -558,9 +569,10 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
             const int64_t* ptb = a.pt + b * a.pt_stride_b;
             int64_t win = tb0;   // first tile of the page-id window held in registers
             int64_t pid = (win + lane < tb1) ? __ldg(ptb + win + lane) : 0;
+            int rid = map_row(a, pid, b);   // the sequence's row in that page
             for (int64_t t0 = tb0; t0 < tb1; t0 += wph) {
                 const int ntile = (int)(tb1 - t0 < wph ? tb1 - t0 : wph);
-                int32_t ph[kComputeWarps];
+                int32_t ph[kComputeWarps], rw[kComputeWarps];
 #pragma unroll
                 for (int s = 0; s < kComputeWarps; ++s) {
                     if (s < ntile) {
@@ -568,14 +580,23 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                         if (t >= win + 32) {   // slide the window (uniform across lanes)
                             win = t;
                             pid = (win + lane < tb1) ? __ldg(ptb + win + lane) : 0;
+                            rid = map_row(a, pid, b);
                         }
                         int64_t v = __shfl_sync(0xffffffffu, pid, (int)(t - win));
+                        int r = __shfl_sync(0xffffffffu, rid, (int)(t - win));
                         if (app_new_page && t == new_tile) {
-                            // the appended token opens a page: take the free stack's top
+                            // the appended token opens a page: take the free stack's top;
+                            // every sequence's rows of it are its own
                             v = __ldg(a.free_stack + a.free_top - 1);
-                            if (lane == 0) a.pt_w[b * a.pt_stride_b + t] = v;
+                            r = (int)b;
+                            if (lane == 0) {
+                                a.pt_w[b * a.pt_stride_b + t] = v;
+                                if (a.row_map && v >= 0 && v < a.num_slots)
+                                    a.row_map[v * a.B + b] = (int32_t)b;
+                            }
                         }
                         ph[s] = (v < 0 || v >= a.num_slots) ? -1 : (int32_t)v;
+                        rw[s] = r;
                     }
                 }
                 const bool ok = mbar_wait(&sm.empty[slot], par ^ 1u, a.err, &sm.abort);
@@ -593,7 +614,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
                         int cc[3];
 #pragma unroll
                         for (int k = 0; k < 3; ++k)
-                            cc[k] = a.role[k] == 0 ? 0 : a.role[k] == 1 ? (int)b : phys;
+                            cc[k] = a.role[k] == 0 ? 0 : a.role[k] == 1 ? rw[s] : phys;
                         uint8_t* tile = st + s * a.tile_bytes;
 #pragma unroll
                         for (int hf = 0; hf < HALVES; ++hf) {
@@ -1536,6 +1557,7 @@ static cudaError_t launch_t(const FusedParams& f, const Plan& pl, CUtensorMapDat
     constexpr bool kMmaLayout = GP == 8 || MODE == 1 || MODE == 2;
     a.pw = (kMmaLayout && f.B == 1 && pl.wph > 1 && f.attend) ? 1 : pl.wph;
     a.pt = f.page_table; a.pt_stride_b = f.pt_stride_b; a.num_slots = f.num_slots;
+    a.row_map = f.row_map;
     a.sal = f.sal; a.sal_stride_b = f.sal_stride_b; a.sal_stride_p = f.sal_stride_p;
     a.scale_r = f.scale_r; a.logit_log2 = f.logit_mul * 1.4426950408889634f;
     a.decay = f.decay; a.omd = f.one_minus_decay;

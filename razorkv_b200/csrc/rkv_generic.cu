@@ -53,6 +53,7 @@ score_kernel(ScoreParams p) {
     const float scale = p.scale_r;
     TokenMap tm{p.page_table ? p.page_table + (int64_t)b * p.pt_stride_b : nullptr,
                 p.page_size, p.stride_p, p.stride_t};
+    tm.row_map = p.row_map; tm.batch = p.B; tm.seq = b; tm.stride_b = p.stride_b;
 
     for (int h = 0; h < p.Hkv; ++h) {
         for (int r0 = 0; r0 < rows_per_head; r0 += chunk_rows) {
@@ -146,6 +147,7 @@ attn_split_kernel(AttnParams p) {
     float m = -INFINITY, l = 0.0f;
     TokenMap tm{p.page_table ? p.page_table + (int64_t)b * p.pt_stride_b : nullptr,
                 p.page_size, p.stride_p, p.stride_t, p.num_slots};
+    tm.row_map = p.row_map; tm.batch = p.B; tm.seq = b; tm.stride_b = p.stride_b;
     const int64_t base = (int64_t)b * p.stride_b + (int64_t)kvh * p.stride_h;
     for (int64_t t = s0; t < s1; ++t) {
         const int64_t off = base + tm.offset(t);
@@ -475,7 +477,12 @@ append_kernel(AppendParams p) {
     const int64_t phys = active ? append_phys(p, t) : 0;
     if (active && h0 == 0 && j == 0 && b == 0 && t % P == 0) {
         const int64_t lp = t / P;
-        if (lp >= (p.pos + P - 1) / P) p.page_table[lp] = phys;
+        if (lp >= (p.pos + P - 1) / P) {
+            p.page_table[lp] = phys;
+            // a page from the free stack starts with every sequence in its own row
+            if (p.row_map)
+                for (int64_t bb = 0; bb < p.B; ++bb) p.row_map[phys * p.B + bb] = (int32_t)bb;
+        }
     }
     const int eb = elt_bytes(p.dtype);
     const int ch = 16 / eb;
@@ -574,8 +581,18 @@ __global__ void compact_tokens_kernel(CompactTokensParams p) {
     const int64_t src_t = compact_source(p, i);
     const int64_t src_pg = p.old_pt[src_t / P];
     const int64_t dst_pg = p.free_stack[p.free_top - 1 - i / P];
-    if (b == 0 && h == 0 && dq == 0 && i % P == 0) p.new_pt[i / P] = dst_pg;
-    const int64_t so = b * p.stride_b + h * p.stride_h + src_pg * p.stride_p + (src_t % P) * p.stride_t;
+    if (b == 0 && h == 0 && dq == 0 && i % P == 0) {
+        p.new_pt[i / P] = dst_pg;
+        // the new pages (from the free stack) hold every sequence in its own row
+        if (p.row_map)
+            for (int64_t bb = 0; bb < p.B; ++bb) p.row_map[dst_pg * p.B + bb] = (int32_t)bb;
+    }
+    int64_t src_row = b;
+    if (p.row_map) {
+        const int64_t r = p.row_map[src_pg * p.B + b];
+        if (r >= 0 && r < p.B) src_row = r;
+    }
+    const int64_t so = src_row * p.stride_b + h * p.stride_h + src_pg * p.stride_p + (src_t % P) * p.stride_t;
     const int64_t dof = b * p.stride_b + h * p.stride_h + dst_pg * p.stride_p + (i % P) * p.stride_t;
     const int eb = elt_bytes(p.dtype);
     for (int64_t e = dq * 4; e < min(D, dq * 4 + 4); ++e) {
@@ -612,6 +629,7 @@ __global__ void gather_kernel(GatherParams p) {
     const int64_t b = r / p.Hkv;
     TokenMap tm{p.page_table ? p.page_table + b * p.pt_stride_b : nullptr, p.page_size,
                 p.stride_p, p.stride_t};
+    tm.row_map = p.row_map; tm.batch = p.B; tm.seq = b; tm.stride_b = p.stride_b;
     const int64_t off = b * p.stride_b + h * p.stride_h + tm.offset(t) + d;
     if (elt_bytes(p.dtype) == 4)
         static_cast<float*>(p.dst)[gid] = static_cast<const float*>(p.src)[off];
@@ -639,8 +657,52 @@ __global__ void gather_kernel(GatherParams p) {
 constexpr int kReindexThreads = 256;
 constexpr int kReindexSmem = 48 * 1024;   // per CTA: moving-row lists + staged chunks
 
+// two (destination, source) row lists: the salience's, and the K/V rows of a moved slot
 __host__ __device__ inline int64_t reindex_list_bytes(int64_t dst_B) {
-    return ((dst_B * 8 + 15) / 16) * 16;
+    return ((dst_B * 16 + 15) / 16) * 16;
+}
+
+// Moving rows in ascending destination order: act_dst[j] <- act_src[j]; returns their count
+// (the same in every thread; all threads must call it).  slot < 0: rows index[b] (the
+// salience, or K and V without a row map); slot >= 0: the physical K/V rows of that slot,
+// row_map[slot][index[b]].  In place, a row that would copy onto itself is left out.
+__device__ int reindex_lists(const ReindexParams& p, int64_t slot, int* act_dst, int* act_src,
+                             int* warp_count, bool report) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int n = 0;
+    for (int b0 = 0; b0 < p.dst_B; b0 += kReindexThreads) {
+        const int b = b0 + threadIdx.x;
+        int src = -1;
+        if (b < p.dst_B) {
+            const int64_t s = p.index[b];
+            if (s < 0 || s >= p.src_B) {
+                if (report) atomicExch(p.err, 2);
+            } else {
+                int64_t r = s;
+                if (slot >= 0) {
+                    const int64_t m = p.row_map[slot * p.src_B + s];
+                    if (m >= 0 && m < p.src_B) r = m;
+                }
+                if (!(p.in_place && r == b)) src = (int)r;
+            }
+        }
+        const unsigned ballot = __ballot_sync(0xffffffffu, src >= 0);
+        if (lane == 0) warp_count[warp] = __popc(ballot);
+        __syncthreads();
+        int before = 0, all = 0;
+        for (int w = 0; w < kReindexThreads / 32; ++w) {
+            before += w < warp ? warp_count[w] : 0;
+            all += warp_count[w];
+        }
+        if (src >= 0) {
+            const int pos = n + before + __popc(ballot & ((1u << lane) - 1u));
+            act_dst[pos] = b;
+            act_src[pos] = src;
+        }
+        n += all;
+        __syncthreads();
+    }
+    return n;
 }
 
 // Threads split into rows_per_pass groups of lanes_per_row lanes; lane e of a group handles
@@ -690,58 +752,76 @@ template <typename T>
 __global__ void __launch_bounds__(kReindexThreads, 4) reindex_kernel(ReindexParams p) {
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ int warp_count[kReindexThreads / 32];
-    int* act_dst = reinterpret_cast<int*>(smem);
-    int* act_src = act_dst + p.dst_B;
+    int* lst_dst = reinterpret_cast<int*>(smem);      // rows by index (salience; K/V unmapped)
+    int* lst_src = lst_dst + p.dst_B;
+    int* map_dst = lst_src + p.dst_B;                 // K/V rows of one slot through the map
+    int* map_src = map_dst + p.dst_B;
     unsigned char* stage = smem + reindex_list_bytes(p.dst_B);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const bool report = blockIdx.x == 0 && p.err;
-    // moving rows, ascending b: (destination row, source row)
-    int n_act = 0;
-    for (int b0 = 0; b0 < p.dst_B; b0 += kReindexThreads) {
-        const int b = b0 + threadIdx.x;
-        int src = -1;
-        if (b < p.dst_B) {
-            const int64_t s = p.index[b];
-            if (s < 0 || s >= p.src_B) {
-                if (report) atomicExch(p.err, 2);
-            } else if (!(p.in_place && s == b)) {
-                src = (int)s;
-            }
-        }
-        const unsigned ballot = __ballot_sync(0xffffffffu, src >= 0);
-        if (lane == 0) warp_count[warp] = __popc(ballot);
-        __syncthreads();
-        int before = 0, all = 0;
-        for (int w = 0; w < kReindexThreads / 32; ++w) {
-            before += w < warp ? warp_count[w] : 0;
-            all += warp_count[w];
-        }
-        if (src >= 0) {
-            const int pos = n_act + before + __popc(ballot & ((1u << lane) - 1u));
-            act_dst[pos] = b;
-            act_src[pos] = src;
-        }
-        n_act += all;
-        __syncthreads();
-    }
-    if (n_act == 0) return;
+    const int n_lst = reindex_lists(p, -1, lst_dst, lst_src, warp_count, blockIdx.x == 0 && p.err);
+    if (n_lst == 0 && (p.row_map == nullptr || p.n_moved == 0)) return;
+    // items: every chunk of the first n_moved slots, then the salience chunks of the others
+    // (their K/V stay; the row map is rewritten)
     const int64_t ych = p.chunks[0] + p.chunks[1] + p.chunks[2];
-    const int64_t items = p.n_listed * ych;
+    const int64_t items_kv = p.n_moved * ych;
+    const int64_t items = items_kv + (p.n_listed - p.n_moved) * p.chunks[2];
+    int64_t mapped_slot = -1;   // slot whose mapped lists are in map_dst / map_src
+    int n_map = 0;
     for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
-        const int64_t li = it / ych;
-        int64_t c = it - li * ych;
+        int64_t li, c;
+        if (it < items_kv) {
+            li = it / ych;
+            c = it - li * ych;
+        } else {
+            const int64_t r = it - items_kv;
+            li = p.n_moved + r / p.chunks[2];
+            c = p.chunks[0] + p.chunks[1] + r % p.chunks[2];
+        }
         const int64_t slot = p.slots[li];
         if (slot < 0 || slot >= p.num_slots) {
-            if (threadIdx.x == 0 && c == 0 && p.err) atomicExch(p.err, 2);
+            if (threadIdx.x == 0 && p.err) atomicExch(p.err, 2);
             continue;
         }
         int which = 0;
         while (which < 2 && c >= p.chunks[which]) { c -= p.chunks[which]; ++which; }
+        const int* ad = lst_dst;
+        const int* as = lst_src;
+        int n = n_lst;
+        if (which < 2 && p.row_map) {
+            if (slot != mapped_slot) {
+                n_map = reindex_lists(p, slot, map_dst, map_src, warp_count, false);
+                mapped_slot = slot;
+            }
+            ad = map_dst; as = map_src; n = n_map;
+        }
+        if (n == 0) continue;
         const int64_t off = c * p.chunk;
         const int len = (int)min(p.chunk, p.row_bytes[which] - off);
-        reindex_rows<T>(p, which, slot, off, len, act_dst, act_src, n_act,
-                        reinterpret_cast<T*>(stage));
+        reindex_rows<T>(p, which, slot, off, len, ad, as, n, reinterpret_cast<T*>(stage));
         __syncthreads();   // the next item restages
+    }
+}
+
+// In-place rewrite of the listed slots' row map after their rows were reindexed: moved slots
+// (the first n_moved) now hold sequence b in row b; the others keep their K/V and map
+// sequence b to the row sequence index[b] used.  A CTA takes a slot at a time, reads all of
+// its new entries before writing any.
+__global__ void __launch_bounds__(256) row_map_compose_kernel(int32_t* row_map, int64_t B,
+                                                               const int64_t* index,
+                                                               const int64_t* slots,
+                                                               int64_t n_listed, int64_t n_moved,
+                                                               int64_t num_slots) {
+    extern __shared__ int32_t nrow[];
+    for (int64_t li = blockIdx.x; li < n_listed; li += gridDim.x) {
+        const int64_t slot = slots[li];
+        if (slot < 0 || slot >= num_slots) continue;
+        int32_t* m = row_map + slot * B;
+        for (int64_t b = threadIdx.x; b < B; b += blockDim.x) {
+            const int64_t s = index[b];
+            nrow[b] = li < n_moved ? (int32_t)b : (s >= 0 && s < B) ? m[s] : m[b];
+        }
+        __syncthreads();
+        for (int64_t b = threadIdx.x; b < B; b += blockDim.x) m[b] = nrow[b];
+        __syncthreads();
     }
 }
 
@@ -984,8 +1064,19 @@ int64_t reindex_chunk_bytes(int64_t dst_B, int64_t max_row_bytes, int vec) {
     return chunk < row ? chunk : row;
 }
 
+cudaError_t launch_row_map_compose(int32_t* row_map, int64_t B, const int64_t* index,
+                                   const int64_t* slots, int64_t n_listed, int64_t n_moved,
+                                   int64_t num_slots, cudaStream_t st) {
+    if (n_listed == 0 || B == 0) return cudaSuccess;
+    const int64_t ctas = n_listed < 4096 ? n_listed : 4096;
+    row_map_compose_kernel<<<(unsigned)ctas, 256, (size_t)(B * 4), st>>>(
+        row_map, B, index, slots, n_listed, n_moved, num_slots);
+    return counted(cudaGetLastError(), 1);
+}
+
 cudaError_t launch_reindex(const ReindexParams& p, cudaStream_t st) {
-    const int64_t items = p.n_listed * (p.chunks[0] + p.chunks[1] + p.chunks[2]);
+    const int64_t items = p.n_moved * (p.chunks[0] + p.chunks[1] + p.chunks[2]) +
+                          (p.n_listed - p.n_moved) * p.chunks[2];
     if (items == 0 || p.dst_B == 0) return cudaSuccess;
     const size_t smem = (size_t)(reindex_list_bytes(p.dst_B) + p.dst_B * p.chunk);
     void (*kern)(ReindexParams) = p.vec == 16 ? reindex_kernel<uint4>

@@ -57,6 +57,7 @@ struct ScoreParams {
     float scale_r, decay, one_minus_decay; int ewma;
     int rows_per_chunk;
     Exchange xc;   // x != nullptr: write keys, leave the salience
+    const int32_t* row_map;   // optional pool row map (rkv_kv_layout.row_map)
 };
 
 struct AttnParams {
@@ -68,6 +69,7 @@ struct AttnParams {
     float scale; int causal;
     void* out; int out_dtype; int64_t o_stride_b, o_stride_h, o_stride_t;
     float* workspace; int num_splits;
+    const int32_t* row_map;   // optional pool row map (rkv_kv_layout.row_map)
 };
 
 struct PageScoreParams {
@@ -87,6 +89,8 @@ struct AppendParams {
     int salience_init;
     int vec_ok;   // every row 16-byte aligned and D a whole number of 16-byte chunks
     Exchange xc;  // x != nullptr: write the new tokens' kv-head norms, leave the salience
+    int32_t* row_map;   // optional pool row map (rkv_kv_layout.row_map); slots taken
+                        // from the free stack get identity entries
 };
 
 // rkv_salience_apply: the salience update of a head-sharded step from the reduced exchange.
@@ -105,6 +109,8 @@ struct CompactTokensParams {
     const int64_t* old_pt; int64_t* new_pt; const int64_t* free_stack; int64_t free_top;
     int64_t new_len, sink, n_kept, sel_page_size, hay_start, tail_src_start;
     const int64_t* kept;
+    int32_t* row_map;   // optional pool row map (rkv_kv_layout.row_map); slots taken
+                        // from the free stack get identity entries
 };
 
 struct GatherParams {
@@ -112,6 +118,7 @@ struct GatherParams {
     int64_t stride_b, stride_h, stride_p, stride_t, page_size;
     const int64_t* page_table; int64_t pt_stride_b;
     const float* sal; int64_t sal_stride_b, sal_stride_p; float* sal_dst;
+    const int32_t* row_map;   // optional pool row map (rkv_kv_layout.row_map)
 };
 
 // Batch reindex of listed pool slots (K, V, salience): row b of dst <- row index[b] of src.
@@ -127,8 +134,13 @@ struct ReindexParams {
     const int64_t* index;       // [dst_B]
     const int64_t* slots; int64_t n_listed;
     int* err;                   // optional: 2 on a slot or index out of range
-    int in_place;               // src == dst: rows whose index is their own are skipped
+    int in_place;               // src == dst: rows that would copy onto themselves are skipped
     int vec;                    // bytes per access: 16, 4 or 2
+    // source row map ([slots][src_B] int32, nullptr = identity): row b of dst <- physical row
+    // row_map[slot][index[b]] of src.  Only the first n_moved listed slots move their K and V;
+    // the salience of every listed slot moves.
+    const int32_t* row_map;
+    int64_t n_moved;
 };
 
 // Fused score + attention for the sm_100a fast path (rkv_decode_sm100.cu).
@@ -156,6 +168,8 @@ struct FusedParams {
     // score-only pass of a compacting step: page scores [B][pool_num] (row stride pool_num)
     // of logical pages pool_first .. pool_first + pool_num - 1 (pool == nullptr: none)
     float* pool; int64_t pool_first, pool_num;
+    int32_t* row_map;   // optional pool row map (rkv_kv_layout.row_map); slots taken
+                        // from the free stack get identity entries
 };
 
 cudaError_t launch_score(const ScoreParams& p, cudaStream_t st);
@@ -183,6 +197,11 @@ cudaError_t launch_gather(const GatherParams& p, cudaStream_t st);
 // chunk size for a reindex into dst_B rows (0: dst_B too large for the staging buffer)
 int64_t reindex_chunk_bytes(int64_t dst_B, int64_t max_row_bytes, int vec);
 cudaError_t launch_reindex(const ReindexParams& p, cudaStream_t st);
+// rewrites the row map of listed slots in place: the first n_moved get identity entries,
+// the rest row_map[s][b] <- row_map[s][index[b]] (entries with an index outside [0, B) stay)
+cudaError_t launch_row_map_compose(int32_t* row_map, int64_t B, const int64_t* index,
+                                   const int64_t* slots, int64_t n_listed, int64_t n_moved,
+                                   int64_t num_slots, cudaStream_t st);
 cudaError_t launch_apply(const ApplyParams& p, cudaStream_t st);
 cudaError_t launch_apply_peer(const PeerApplyParams& p, cudaStream_t st);
 

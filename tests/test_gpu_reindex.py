@@ -21,10 +21,11 @@ def _pool(slots, B, Hkv, P, D, dtype, seed):
     return k, v, s
 
 
-def _layout(k, v):
+def _layout(k, v, row_map=None):
     slots, B, Hkv, P, D = k.shape
     return KVLayout(k.data_ptr(), v.data_ptr(), dtype_code(k.dtype), D, B, Hkv, k.stride(1),
-                    k.stride(2), k.stride(0), k.stride(3), P, slots, None, 0, 0)
+                    k.stride(2), k.stride(0), k.stride(3), P, slots, None, 0, 0,
+                    row_map.data_ptr() if row_map is not None else None)
 
 
 def _sal(s):
@@ -37,12 +38,14 @@ def _flag():
     return f
 
 
-def _reindex(src, dst, index, slots, flag=None):
+def _reindex(src, dst, index, slots, flag=None, row_map=None, num_moved=None):
     lib = _lib.load()
     idx = torch.as_tensor(index, dtype=torch.int64).cuda()
     sl = torch.as_tensor(slots, dtype=torch.int64).cuda()
-    st = lib.rkv_reindex_batch(_layout(*src[:2]), _sal(src[2]), _layout(*dst[:2]), _sal(dst[2]),
-                               idx.data_ptr(), sl.data_ptr(), sl.numel(),
+    moved = sl.numel() if num_moved is None else num_moved
+    st = lib.rkv_reindex_batch(_layout(*src[:2], row_map), _sal(src[2]),
+                               _layout(*dst[:2], row_map if dst is src else None), _sal(dst[2]),
+                               idx.data_ptr(), sl.data_ptr(), sl.numel(), moved,
                                flag.data_ptr() if flag is not None else None,
                                stream_ptr(torch.device("cuda")))
     torch.cuda.synchronize()
@@ -138,17 +141,17 @@ def test_rejected_calls_launch_nothing():
     # K in place but V not
     bad = _layout(k, v2)
     assert lib.rkv_reindex_batch(_layout(k, v), _sal(s), bad, _sal(s2), idx.data_ptr(),
-                                 sl.data_ptr(), 1, None, None) == 1
+                                 sl.data_ptr(), 1, 1, None, None) == 1
     # non-contiguous (slot, sequence) planes
     lay = _layout(k, v)
     lay.stride_h = lay.stride_h * 2
     assert lib.rkv_reindex_batch(lay, _sal(s), _layout(k2, v2), _sal(s2), idx.data_ptr(),
-                                 sl.data_ptr(), 1, None, None) == 2
+                                 sl.data_ptr(), 1, 1, None, None) == 2
     # a destination batch too large for the staging buffer
     big = _layout(k2, v2)
     big.batch = 100000
     assert lib.rkv_reindex_batch(_layout(k, v), _sal(s), big, _sal(s2), idx.data_ptr(),
-                                 sl.data_ptr(), 1, None, None) == 2
+                                 sl.data_ptr(), 1, 1, None, None) == 2
     assert lib.rkv_launch_count() == n0
 
 
@@ -167,8 +170,14 @@ def test_cache_reorder_touches_live_pages_only():
     K0 = [cache.key_cache[l].clone() for l in range(2)]
     S0 = [cache.salience_scores[l].clone() for l in range(2)]
     ptr = cache._k.data_ptr()
+    pool0 = cache._k.clone()
+    full = torch.cat([cache.page_table(l)[:-1] for l in range(2)])
     cache.reorder_cache(torch.tensor([2, 2, 0]))
     assert cache._k.data_ptr() == ptr
+    # full pages keep their K (only the row map changed); the salience moved
+    assert torch.equal(cache._k[full], pool0[full])
+    assert torch.equal(cache._rowmap[full].cpu(), torch.tensor([[2, 2, 0]] * full.numel(),
+                                                               dtype=torch.int32))
     for l in range(2):
         assert torch.equal(cache.key_cache[l], K0[l][[2, 2, 0]])
         assert torch.equal(cache.salience_scores[l], S0[l][[2, 2, 0]])
@@ -176,4 +185,107 @@ def test_cache_reorder_touches_live_pages_only():
     assert cache.batch_size == 6
     for l in range(2):
         assert torch.equal(cache.key_cache[l], K0[l][[2, 2, 2, 2, 0, 0]])
+    cache.check_errors()
+
+
+def test_row_map_moves_listed_pages_and_rewrites_the_rest():
+    """In place with a row map: the first num_moved slots get their K/V rows gathered through
+    the map (and identity entries); the others keep K/V and compose their map entries; the
+    salience of every listed slot moves."""
+    slots, B, Hkv, P, D, dt = 24, 6, 2, 16, 128, torch.bfloat16
+    rng = np.random.default_rng(5)
+    pool = _pool(slots, B, Hkv, P, D, dt, seed=4)
+    rm0 = torch.as_tensor(rng.integers(0, B, size=(slots, B)), dtype=torch.int32).cuda()
+    rm = rm0.clone()
+    live = rng.permutation(slots)[:15]
+    moved, kept = live[:4], live[4:]
+    index = rng.integers(0, B, size=B)
+    before = [t.clone() for t in pool]
+    flag = _flag()
+    assert _reindex(pool, pool, index, live, flag, row_map=rm, num_moved=len(moved)) == 0
+    assert int(flag.item()) == 0
+    k0, v0, s0 = before
+    idx = torch.as_tensor(index).cuda()
+    for sl in moved:
+        rows = rm0[sl].long()[idx]
+        assert torch.equal(pool[0][sl], k0[sl][rows])
+        assert torch.equal(pool[1][sl], v0[sl][rows])
+        assert torch.equal(rm[sl].cpu(), torch.arange(B, dtype=torch.int32))
+    for sl in kept:
+        assert torch.equal(pool[0][sl], k0[sl]) and torch.equal(pool[1][sl], v0[sl])
+        assert torch.equal(rm[sl], rm0[sl][idx])
+    for sl in live:
+        assert torch.equal(pool[2][sl], s0[sl][idx])
+    rest = np.setdiff1d(np.arange(slots), live)
+    for t, t0 in zip(pool, before):
+        assert torch.equal(t[rest], t0[rest])
+    assert torch.equal(rm[rest], rm0[rest])
+    # out of place through the map: the new pool holds the mapped rows as its own rows
+    dst = [torch.zeros(slots, 3, Hkv, P, D, dtype=dt, device="cuda"),
+           torch.zeros(slots, 3, Hkv, P, D, dtype=dt, device="cuda"),
+           torch.zeros(slots, 3, P, device="cuda")]
+    assert _reindex(pool, dst, [5, 0, 5], live, row_map=rm) == 0
+    sel = torch.tensor([5, 0, 5]).cuda()
+    for sl in live:
+        rows = rm[sl].long()[sel]
+        assert torch.equal(dst[0][sl], pool[0][sl][rows])
+        assert torch.equal(dst[2][sl], pool[2][sl][sel])
+
+
+def test_beam_search_on_shared_pages_matches_oracle():
+    """reorder_cache as a page-table update across decode steps, compactions and a crop: the
+    cache keeps the oracle's K, V and salience (the oracle copies rows) bit for bit."""
+    from oracle import razorkv_oracle as O
+    layers, B, Hq, Hkv, D = 2, 4, 8, 2, 128
+    dt = torch.bfloat16
+    rc = RazorConfig(compression_ratio=0.30, sink_tokens=32, local_window=64, page_size=16,
+                     pyramid_mode="uniform")
+    cache = PagedRazorKVCache(rc, layers)
+    oc = O.OracleCache(O.OracleConfig(compression_ratio=0.30, sink_tokens=32, local_window=64,
+                                      page_size=16, pyramid_mode="uniform"), layers, 2)
+
+    def randn(*shape, seed):
+        return torch.randn(*shape, generator=torch.Generator().manual_seed(seed)).to(dt).cuda()
+
+    def check(where):
+        for l in range(layers):
+            assert np.array_equal(cache.key_cache[l].float().cpu().numpy(), oc.K[l]), where
+            assert np.array_equal(cache.value_cache[l].float().cpu().numpy(), oc.V[l]), where
+            S = cache.salience_scores[l].cpu().numpy()
+            assert np.array_equal(S.view(np.uint32), oc.S[l].view(np.uint32)), where
+
+    for l in range(layers):
+        k, v = randn(B, Hkv, 600, D, seed=l), randn(B, Hkv, 600, D, seed=40 + l)
+        q = randn(B, Hq, 1, D, seed=80 + l)
+        cache.update(k, v, l, {"query_states": q})
+        oc.update(k.float().cpu().numpy(), v.float().cpu().numpy(), l, q.float().cpu().numpy())
+    rng = np.random.default_rng(9)
+    seed = 1000
+    compactions0 = cache.compactions
+    for step in range(48):
+        for l in range(layers):
+            seed += 3
+            q = randn(B, Hq, 1, D, seed=seed)
+            k, v = randn(B, Hkv, 1, D, seed=seed + 1), randn(B, Hkv, 1, D, seed=seed + 2)
+            out = cache.decode_step(q, k, v, l)
+            Kc, Vc = oc.update(k.float().cpu().numpy(), v.float().cpu().numpy(), l,
+                               q.float().cpu().numpy())
+            ref = O.attention(q.float().cpu().numpy(), Kc, Vc)
+            np.testing.assert_allclose(out.float().cpu().numpy(), ref, atol=2e-2, rtol=1e-2)
+        beam = np.sort(rng.integers(0, B, size=B))
+        cache.reorder_cache(torch.as_tensor(beam))
+        for l in range(layers):
+            for arr in (oc.K, oc.V, oc.S):
+                arr[l] = np.ascontiguousarray(arr[l][beam])
+        if step == 20:
+            cache.crop(3)
+            for l in range(layers):
+                oc.K[l], oc.V[l] = oc.K[l][:, :, :-3].copy(), oc.V[l][:, :, :-3].copy()
+                oc.S[l] = oc.S[l][:, :-3].copy()
+                oc.ids[l] = oc.ids[l][:-3]
+            oc.seen -= 3
+        if step % 8 == 0:
+            check(f"step {step}")
+    check("end")
+    assert cache.compactions > compactions0   # pages were dropped while shared
     cache.check_errors()
