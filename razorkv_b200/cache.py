@@ -157,6 +157,11 @@ class _LayerList(list):
 
 
 class PagedRazorKVCache(BaseCacheClass):
+    # reorder_cache with the batch size unchanged (beam search) shares pages between sequences
+    # through the row map; set False to move every live page's K/V rows instead, which keeps
+    # the pool in sequence order for code that reads it without the row map
+    share_pages_on_reorder: bool = True
+
     def __init__(self, config: Optional[RazorConfig] = None, num_layers: int = 32,
                  max_slots: Optional[int] = None):
         try:
@@ -1082,6 +1087,9 @@ class PagedRazorKVCache(BaseCacheClass):
         idx = index.to(device=self._device, dtype=torch.int64).reshape(-1).contiguous()
         new_b = idx.numel()
         slots, n_last = self._live_slots()
+        if new_b == self._B and not self.share_pages_on_reorder:
+            self._reindex_rows(idx, slots, slots.numel())
+            return
         if new_b == self._B:
             if self._rowmap is None:
                 self._rowmap = torch.arange(self._B, dtype=torch.int32,

@@ -142,3 +142,34 @@ def test_paged_attention_generates_the_same_tokens():
                                        pad_token_id=0))
         RazorEngine.unpatch_model(model)
     assert torch.equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("dtype,hidden,heads,kv_heads", [
+    (torch.float32, 256, 4, 2),       # head_dim 64: shape-general kernels
+    (torch.bfloat16, 512, 4, 1),      # head_dim 128: the sm_100a decode kernel
+])
+def test_beam_search_on_shared_pages(dtype, hidden, heads, kv_heads, monkeypatch):
+    """HF beam search calls reorder_cache every step.  Sharing pages through the row map must
+    generate exactly what moving the rows generates (same tokens, same beam scores), with
+    compactions during the search."""
+    model = _llama(hidden, heads, kv_heads, 2, vocab=256, dtype=dtype, seed=5)
+    rcfg = RazorConfig(compression_ratio=0.30, sink_tokens=16, local_window=32, page_size=16)
+    prompt = torch.randint(1, 256, (2, 300), generator=torch.Generator().manual_seed(6)).cuda()
+    runs = []
+    for share in (True, False):
+        monkeypatch.setattr(PagedRazorKVCache, "share_pages_on_reorder", share)
+        RazorEngine.patch_model(model, config=rcfg)
+        with torch.no_grad():
+            out = model.generate(prompt, attention_mask=torch.ones_like(prompt), num_beams=3,
+                                 max_new_tokens=40, do_sample=False, eos_token_id=None,
+                                 pad_token_id=0, return_dict_in_generate=True,
+                                 output_scores=True)
+        RazorEngine.unpatch_model(model)
+        cache = out.past_key_values
+        assert isinstance(cache, PagedRazorKVCache)
+        assert (cache._rowmap is not None) == share
+        assert cache.compactions > 2 * 2   # prefill compactions plus decode-time ones
+        cache.check_errors()
+        runs.append(out)
+    assert torch.equal(runs[0].sequences, runs[1].sequences)
+    assert torch.equal(runs[0].sequences_scores, runs[1].sequences_scores)
