@@ -232,11 +232,13 @@ def test_row_map_moves_listed_pages_and_rewrites_the_rest():
         assert torch.equal(dst[2][sl], pool[2][sl][sel])
 
 
-def test_beam_search_on_shared_pages_matches_oracle():
+@pytest.mark.parametrize("Hq", [8, 14], ids=["gqa4", "gqa7_screened"])
+def test_beam_search_on_shared_pages_matches_oracle(Hq):
     """reorder_cache as a page-table update across decode steps, compactions and a crop: the
-    cache keeps the oracle's K, V and salience (the oracle copies rows) bit for bit."""
+    cache keeps the oracle's K, V and salience (the oracle copies rows) bit for bit, on the
+    4-head instance and on the screened instance of 5-8 query heads per kv head."""
     from oracle import razorkv_oracle as O
-    layers, B, Hq, Hkv, D = 2, 4, 8, 2, 128
+    layers, B, Hkv, D = 2, 4, 2, 128
     dt = torch.bfloat16
     rc = RazorConfig(compression_ratio=0.30, sink_tokens=32, local_window=64, page_size=16,
                      pyramid_mode="uniform")
