@@ -674,10 +674,14 @@ __device__ int reindex_lists(const ReindexParams& p, int64_t slot, int* act_dst,
         const int b = b0 + threadIdx.x;
         int src = -1;
         if (b < p.dst_B) {
-            const int64_t s = p.index[b];
-            if (s < 0 || s >= p.src_B) {
-                if (report) atomicExch(p.err, 2);
-            } else {
+            int64_t s = p.index[b];
+            const bool bad = s < 0 || s >= p.src_B;
+            if (bad && report) atomicExch(p.err, 2);
+            // a bad index leaves the sequence as it was: through a row map its own row moves
+            // into row b (the slot's map becomes identity), without one nothing moves
+            const bool keep = bad && slot >= 0 && b < p.src_B;
+            if (keep) s = b;
+            if (!bad || keep) {
                 int64_t r = s;
                 if (slot >= 0) {
                     const int64_t m = p.row_map[slot * p.src_B + s];

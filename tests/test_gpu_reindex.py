@@ -291,3 +291,31 @@ def test_beam_search_on_shared_pages_matches_oracle(Hq):
     check("end")
     assert cache.compactions > compactions0   # pages were dropped while shared
     cache.check_errors()
+
+
+def test_row_map_bad_index_keeps_the_sequence():
+    """An index outside the batch sets the error flag and leaves that sequence as it was, on
+    moved slots (its own row is gathered into place) and on rewritten ones (its entry stays)."""
+    slots, B, Hkv, P, D, dt = 6, 4, 2, 16, 128, torch.bfloat16
+    rng = np.random.default_rng(8)
+    pool = _pool(slots, B, Hkv, P, D, dt, seed=9)
+    rm0 = torch.as_tensor(rng.integers(0, B, size=(slots, B)), dtype=torch.int32).cuda()
+    rm = rm0.clone()
+    index = [1, 9, 0, 3]
+    ok = [0, 2, 3]
+    before = [t.clone() for t in pool]
+    flag = _flag()
+    assert _reindex(pool, pool, index, list(range(slots)), flag, row_map=rm, num_moved=2) == 0
+    assert int(flag.item()) == 2
+    flag.zero_()
+    k0, _, s0 = before
+    for sl in range(slots):
+        for b in range(B):
+            src = index[b] if b in ok else b
+            assert torch.equal(pool[2][sl][b], s0[sl][src])
+            if sl < 2:
+                assert torch.equal(pool[0][sl][b], k0[sl][int(rm0[sl][src])])
+                assert int(rm[sl][b]) == b
+            else:
+                assert torch.equal(pool[0][sl], k0[sl])
+                assert int(rm[sl][b]) == int(rm0[sl][src])
