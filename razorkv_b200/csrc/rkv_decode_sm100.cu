@@ -570,68 +570,137 @@ decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ C
             int64_t win = tb0;   // first tile of the page-id window held in registers
             int64_t pid = (win + lane < tb1) ? __ldg(ptb + win + lane) : 0;
             int rid = map_row(a, pid, b);   // the sequence's row in that page
-            for (int64_t t0 = tb0; t0 < tb1; t0 += wph) {
-                const int ntile = (int)(tb1 - t0 < wph ? tb1 - t0 : wph);
-                int32_t ph[kComputeWarps], rw[kComputeWarps];
-#pragma unroll
-                for (int s = 0; s < kComputeWarps; ++s) {
-                    if (s < ntile) {
-                        const int64_t t = t0 + s;
-                        if (t >= win + 32) {   // slide the window (uniform across lanes)
-                            win = t;
-                            pid = (win + lane < tb1) ? __ldg(ptb + win + lane) : 0;
-                            rid = map_row(a, pid, b);
-                        }
-                        int64_t v = __shfl_sync(0xffffffffu, pid, (int)(t - win));
-                        int r = __shfl_sync(0xffffffffu, rid, (int)(t - win));
-                        if (app_new_page && t == new_tile) {
-                            // the appended token opens a page: take the free stack's top;
-                            // every sequence's rows of it are its own
-                            v = __ldg(a.free_stack + a.free_top - 1);
-                            r = (int)b;
-                            if (lane == 0) {
-                                a.pt_w[b * a.pt_stride_b + t] = v;
-                                if (a.row_map && v >= 0 && v < a.num_slots)
-                                    a.row_map[v * a.B + b] = (int32_t)b;
-                            }
-                        }
-                        ph[s] = (v < 0 || v >= a.num_slots) ? -1 : (int32_t)v;
-                        rw[s] = r;
+            // Two arrangements of the same stage loop: one tile per lane (the 8-head instances)
+            // or every lane holding all of the stage's tiles (the others).  Each measured the
+            // faster of the two for its instances.
+            if constexpr (GP == 8) {
+                for (int64_t t0 = tb0; t0 < tb1; t0 += wph) {
+                    const int ntile = (int)(tb1 - t0 < wph ? tb1 - t0 : wph);
+                    if (t0 + ntile > win + 32) {   // slide the window (uniform across lanes)
+                        win = t0;
+                        pid = (win + lane < tb1) ? __ldg(ptb + win + lane) : 0;
+                        rid = map_row(a, pid, b);
                     }
-                }
-                const bool ok = mbar_wait(&sm.empty[slot], par ^ 1u, a.err, &sm.abort);
-                if (lane == 0 && ok) {
+                    // lane s < ntile holds tile t0 + s: its slot and the sequence's row in it
+                    const int src = (int)(t0 - win) + (lane < ntile ? lane : 0);
+                    int64_t v = __shfl_sync(0xffffffffu, pid, src);
+                    int r = __shfl_sync(0xffffffffu, rid, src);
+                    if (app_new_page && lane < ntile && t0 + lane == new_tile) {
+                        // the appended token opens a page: take the free stack's top; every
+                        // sequence's rows of it are its own
+                        v = __ldg(a.free_stack + a.free_top - 1);
+                        r = (int)b;
+                        a.pt_w[b * a.pt_stride_b + new_tile] = v;
+                        if (a.row_map && v >= 0 && v < a.num_slots) a.row_map[v * a.B + b] = (int32_t)b;
+                    }
+                    const int ph = (v < 0 || v >= a.num_slots) ? -1 : (int)v;
+                    const bool ok = mbar_wait(&sm.empty[slot], par ^ 1u, a.err, &sm.abort);
+                    // lane 0 records every tile's slot before the arrive that releases them
+    #pragma unroll 1
+                    for (int s = 0; s < ntile; ++s) {
+                        const int ph_s = __shfl_sync(0xffffffffu, ph, s);
+                        if (lane == 0 && ok) {
+                            if (ph_s < 0 && a.err) atomicExch(a.err, 2);
+                            sm.phys[slot][s] = ph_s;
+                        }
+                    }
                     uint8_t* st = smem + slot * a.stage_bytes;
-                    uint32_t bytes = (uint32_t)(ntile * a.tile_bytes);
-                    for (int s = 0; s < ntile; ++s) {
-                        if (ph[s] < 0 && a.err) atomicExch(a.err, 2);
-                        sm.phys[slot][s] = ph[s];
+                    if (lane == 0 && ok) {
+                        uint32_t bytes = (uint32_t)(ntile * a.tile_bytes);
+                        if (a.score && a.sal_bulk) bytes += (uint32_t)(ntile * kTileTokens * 4);
+                        mbar_arrive_expect_tx(&sm.full[slot], bytes);
                     }
-                    if (a.score && a.sal_bulk) bytes += (uint32_t)(ntile * kTileTokens * 4);
-                    mbar_arrive_expect_tx(&sm.full[slot], bytes);
+    #pragma unroll 1
                     for (int s = 0; s < ntile; ++s) {
-                        const int phys = max(ph[s], 0);
-                        int cc[3];
-#pragma unroll
-                        for (int k = 0; k < 3; ++k)
-                            cc[k] = a.role[k] == 0 ? 0 : a.role[k] == 1 ? rw[s] : phys;
-                        uint8_t* tile = st + s * a.tile_bytes;
-#pragma unroll
-                        for (int hf = 0; hf < HALVES; ++hf) {
-                            tma_load_5d(tile + hf * a.half_bytes, &tmk, &sm.full[slot], hf * 64, 0,
-                                        cc[0], cc[1], cc[2]);
-                            if (a.attend)
-                                tma_load_5d(tile + a.kv_tile_bytes + hf * a.half_bytes, &tmv,
-                                            &sm.full[slot], hf * 64, 0, cc[0], cc[1], cc[2]);
+                        const int phys = max(__shfl_sync(0xffffffffu, ph, s), 0);
+                        const int row = __shfl_sync(0xffffffffu, r, s);
+                        if (lane == 0 && ok) {
+                            int cc[3];
+    #pragma unroll
+                            for (int k = 0; k < 3; ++k)
+                                cc[k] = a.role[k] == 0 ? 0 : a.role[k] == 1 ? row : phys;
+                            uint8_t* tile = st + s * a.tile_bytes;
+    #pragma unroll
+                            for (int hf = 0; hf < HALVES; ++hf) {
+                                tma_load_5d(tile + hf * a.half_bytes, &tmk, &sm.full[slot], hf * 64, 0,
+                                            cc[0], cc[1], cc[2]);
+                                if (a.attend)
+                                    tma_load_5d(tile + a.kv_tile_bytes + hf * a.half_bytes, &tmv,
+                                                &sm.full[slot], hf * 64, 0, cc[0], cc[1], cc[2]);
+                            }
+                            if (a.score && a.sal_bulk)
+                                bulk_load(&sm.sal_old[slot][s][0],
+                                          a.sal + (int64_t)phys * a.sal_stride_p + b * a.sal_stride_b,
+                                          kTileTokens * 4, &sm.full[slot]);
                         }
-                        if (a.score && a.sal_bulk)
-                            bulk_load(&sm.sal_old[slot][s][0],
-                                      a.sal + (int64_t)phys * a.sal_stride_p + b * a.sal_stride_b,
-                                      kTileTokens * 4, &sm.full[slot]);
                     }
+                    __syncwarp();
+                    if (++slot == NS) { slot = 0; par ^= 1u; }
                 }
-                __syncwarp();
-                if (++slot == NS) { slot = 0; par ^= 1u; }
+            } else {
+                for (int64_t t0 = tb0; t0 < tb1; t0 += wph) {
+                    const int ntile = (int)(tb1 - t0 < wph ? tb1 - t0 : wph);
+                    int32_t ph[kComputeWarps], rw[kComputeWarps];
+    #pragma unroll
+                    for (int s = 0; s < kComputeWarps; ++s) {
+                        if (s < ntile) {
+                            const int64_t t = t0 + s;
+                            if (t >= win + 32) {   // slide the window (uniform across lanes)
+                                win = t;
+                                pid = (win + lane < tb1) ? __ldg(ptb + win + lane) : 0;
+                                rid = map_row(a, pid, b);
+                            }
+                            int64_t v = __shfl_sync(0xffffffffu, pid, (int)(t - win));
+                            int r = __shfl_sync(0xffffffffu, rid, (int)(t - win));
+                            if (app_new_page && t == new_tile) {
+                                // the appended token opens a page: take the free stack's top;
+                                // every sequence's rows of it are its own
+                                v = __ldg(a.free_stack + a.free_top - 1);
+                                r = (int)b;
+                                if (lane == 0) {
+                                    a.pt_w[b * a.pt_stride_b + t] = v;
+                                    if (a.row_map && v >= 0 && v < a.num_slots)
+                                        a.row_map[v * a.B + b] = (int32_t)b;
+                                }
+                            }
+                            ph[s] = (v < 0 || v >= a.num_slots) ? -1 : (int32_t)v;
+                            rw[s] = r;
+                        }
+                    }
+                    const bool ok = mbar_wait(&sm.empty[slot], par ^ 1u, a.err, &sm.abort);
+                    if (lane == 0 && ok) {
+                        uint8_t* st = smem + slot * a.stage_bytes;
+                        uint32_t bytes = (uint32_t)(ntile * a.tile_bytes);
+                        for (int s = 0; s < ntile; ++s) {
+                            if (ph[s] < 0 && a.err) atomicExch(a.err, 2);
+                            sm.phys[slot][s] = ph[s];
+                        }
+                        if (a.score && a.sal_bulk) bytes += (uint32_t)(ntile * kTileTokens * 4);
+                        mbar_arrive_expect_tx(&sm.full[slot], bytes);
+                        for (int s = 0; s < ntile; ++s) {
+                            const int phys = max(ph[s], 0);
+                            int cc[3];
+    #pragma unroll
+                            for (int k = 0; k < 3; ++k)
+                                cc[k] = a.role[k] == 0 ? 0 : a.role[k] == 1 ? rw[s] : phys;
+                            uint8_t* tile = st + s * a.tile_bytes;
+    #pragma unroll
+                            for (int hf = 0; hf < HALVES; ++hf) {
+                                tma_load_5d(tile + hf * a.half_bytes, &tmk, &sm.full[slot], hf * 64, 0,
+                                            cc[0], cc[1], cc[2]);
+                                if (a.attend)
+                                    tma_load_5d(tile + a.kv_tile_bytes + hf * a.half_bytes, &tmv,
+                                                &sm.full[slot], hf * 64, 0, cc[0], cc[1], cc[2]);
+                            }
+                            if (a.score && a.sal_bulk)
+                                bulk_load(&sm.sal_old[slot][s][0],
+                                          a.sal + (int64_t)phys * a.sal_stride_p + b * a.sal_stride_b,
+                                          kTileTokens * 4, &sm.full[slot]);
+                        }
+                    }
+                    __syncwarp();
+                    if (++slot == NS) { slot = 0; par ^= 1u; }
+                }
             }
             pos = seg_end;
         }
