@@ -113,7 +113,7 @@ def test_config_budget_reference_properties():
                     pyramid_mode="adaptive", pyramid_min_ratio=0.15, pyramid_max_ratio=0.70)
     b0, b16, b31 = (c.get_layer_budget(i, 32, 1000) for i in (0, 16, 31))
     assert b0 <= b16 <= b31 and b0 >= 80
-    # the BASELINE pyramid (linear 15 % -> 70 %) at 32k: layer 0 keeps 4915 tokens, 31 keeps 22937
+    # the Llama-8B-shaped workload's pyramid (linear 15 % -> 70 %) at 32k: layer 0 keeps 4915 tokens, 31 keeps 22937
     lin = RazorConfig(pyramid_mode="linear")
     assert lin.get_layer_budget(0, 32, 32768) == 4915
     assert lin.get_layer_budget(31, 32, 32768) == 22937
